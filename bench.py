@@ -1,0 +1,511 @@
+"""Benchmark: StreamingLLM block-sparse attention on B200 (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload all|fwdbwd|fwd|decode]
+
+Headline (``value``): BASELINE config 2 -- sparse prefill forward+backward,
+B=4, H=32, N=16384, D=128, bf16, S=4, W=2048, BM=BN=128 -- as kept-block
+TFLOP/s (F_fwd = nnz * B * H * 4 * BM * BN * D; fwd+bwd = 3.5 * F_fwd).
+Each rank processes its own B*H = 128 (batch, head) units (weak scaling:
+the job's batch is 4 * N); ``value`` = all ranks' FLOPs / max-over-ranks
+time.  Secondary lines (``extra``): config 3 prefill forward (TFLOP/s) and
+config 4 decode (KV GB/s over the 2.1517e9 visible K/V bytes per step).
+
+``e2e`` runs the same step through the public API from pinned host buffers
+(Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step).
+``roofline`` uses the dominant kernel's duration measured inside the timed
+region with CUDA events recorded by libsbfa around each launch.
+``--impl reference`` times the upstream eager masked-attention algorithm
+(the CPU oracle port) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "graph-kernel-injection_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+CFG2 = dict(B=4, H=32, N=16384, D=128, S=4, W=2048, BM=128, BN=128, dtype=torch.bfloat16)
+CFG3 = dict(B=1, H=32, N=131072, D=128, S=4, W=4096, BM=128, BN=128, dtype=torch.float16)
+CFG4 = dict(B=64, H=32, N=100001, D=128, S=4, W=2048, BM=1, BN=64, dtype=torch.float16)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+class Dist:
+    def __init__(self, want: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if want != self.world:
+            raise SystemExit(f"--gpus {want} but WORLD_SIZE={self.world}")
+        self.pg = None
+
+    def init(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        torch.cuda.set_device(self.local)
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather_checksums(self, vals):
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        if not self.pg:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [o.tolist() for o in out]
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"sbfa_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[2:6]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+
+def kept_blocks(cfg) -> int:
+    import sparse_triton_kernel as stk
+    m = stk.make_streaming_mask(1 if cfg is CFG4 else cfg["N"], cfg["N"],
+                                stk.StreamingMaskSpec(cfg["S"], cfg["W"]), cfg["BM"], cfg["BN"],
+                                device="cuda")
+    return int(m.sum().item()), m
+
+
+def f_fwd(cfg, nnz: int) -> float:
+    return float(nnz) * cfg["B"] * cfg["H"] * 4 * cfg["BM"] * cfg["BN"] * cfg["D"]
+
+
+def decode_bytes(cfg) -> tuple:
+    """(K+V visible bytes, q+o bytes) per decode step for the streaming rule."""
+    qpos = cfg["N"] - 1
+    vis = min(cfg["S"], qpos + 1) + (qpos + 1 - max(min(cfg["S"], qpos + 1), qpos - cfg["W"] + 1))
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+    kv = cfg["B"] * cfg["H"] * 2 * vis * cfg["D"] * es
+    qo = cfg["B"] * cfg["H"] * 2 * cfg["D"] * es
+    return kv, qo
+
+
+# algorithmic FLOPs of one launch, as a multiple of F_fwd (bwd total 2.5 F_fwd:
+# dK/dV kernel = S, dP, dV, dK; dQ kernel = dQ)
+KERNEL_WORK = {"fwd": 1.0, "dkdv": 2.0, "dq": 0.5}
+
+
+def kernel_kind(name: str):
+    for kind in ("dkdv", "dq", "fwd"):
+        if name.startswith(kind):
+            return kind
+    if name.startswith("decode_split"):
+        return "decode"
+    return None
+
+
+def time_steps(dist, step, steps: int, warmup: int):
+    import sbfa_native as native
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    native.timing_read()  # discard warm-up records
+    native.timing(True)
+    n0 = native.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    native.timing(False)
+    launches = native.launch_count() - n0
+    ms = start.elapsed_time(end)
+    per_kernel = native.timing_read()
+    return dist.max(ms), launches, per_kernel
+
+
+def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None):
+    if not per_kernel:
+        return None
+    name, (tot, cnt) = max(per_kernel.items(), key=lambda kv: kv[1][0])
+    kind = kernel_kind(name)
+    avg_s = tot / cnt / 1e3
+    if kind == "decode":
+        achieved = kv_bytes / avg_s / 1e9   # one split launch reads every visible K/V row once
+        peak = pk["hbm_gbs"]
+        unit, bound = "GB/s", "hbm"
+    elif kind in KERNEL_WORK:
+        achieved = KERNEL_WORK[kind] * flops_fwd / avg_s / 1e12
+        peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+        unit, bound = "TFLOP/s", "tensor"
+    else:
+        return None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as fh:
+            traffic = json.load(fh).get(name)
+    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
+            "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
+            "peak_source": f"{peak_src} ({'sustained' if sustained and bound == 'tensor' else 'burst'})",
+            "avg_launch_ms": round(tot / cnt, 4), "launches": cnt,
+            "kernel_share": {k: round(v[0] / sum(x[0] for x in per_kernel.values()), 4)
+                             for k, v in per_kernel.items()}}
+
+
+def make_inputs(cfg, rank: int, n_q=None):
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(rank)
+    mul = 0.5 if cfg is CFG3 else 1.0
+    nq = cfg["N"] if n_q is None else n_q
+    q = torch.randn(cfg["B"], cfg["H"], nq, cfg["D"], generator=g, device=dev,
+                    dtype=cfg["dtype"])
+    k = torch.randn(cfg["B"], cfg["H"], cfg["N"], cfg["D"], generator=g, device=dev,
+                    dtype=cfg["dtype"])
+    v = torch.randn(cfg["B"], cfg["H"], cfg["N"], cfg["D"], generator=g, device=dev,
+                    dtype=cfg["dtype"])
+    if mul != 1.0:
+        for t in (q, k, v):
+            t.mul_(mul)
+    return q, k, v
+
+
+def bench_fwdbwd(dist, args, pk, src):
+    import sparse_triton_kernel as stk
+    cfg = CFG2
+    nnz, mask = kept_blocks(cfg)
+    F = f_fwd(cfg, nnz)
+    q, k, v = make_inputs(cfg, dist.rank)
+    g1 = torch.Generator(device="cuda").manual_seed(1000 + dist.rank)
+    do = torch.randn(q.shape, generator=g1, device="cuda", dtype=cfg["dtype"])
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
+              window_size=cfg["W"])
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        o = stk.block_sparse_attention(q, k, v, mask, **kw)
+        o.backward(do)
+        return o
+
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    ms, launches, per_kernel = time_steps(dist, step, args.steps, args.warmup)
+    clk = clocks.stop()
+    o = step()
+    torch.cuda.synchronize()
+    sums = dist.gather_checksums([float(o.detach().double().sum()),
+                                  float(q.grad.double().abs().sum())])
+    finite = all(math.isfinite(x) for r in sums for x in r)
+    total_flops = 3.5 * F * dist.world * args.steps
+    value = total_flops / (ms / 1e3) / 1e12
+
+    # e2e through the public API from pinned host memory
+    hq, hk, hv, hdo = (t.detach().to("cpu").pin_memory() for t in (q, k, v, do))
+    out_h = [torch.empty(q.shape, dtype=cfg["dtype"]).pin_memory() for _ in range(4)]
+    dq_, dk_, dv_ = (torch.empty_like(t) for t in (q, k, v))
+
+    def e2e_step():
+        qd = hq.to("cuda", non_blocking=True).requires_grad_(True)
+        kd = hk.to("cuda", non_blocking=True).requires_grad_(True)
+        vd = hv.to("cuda", non_blocking=True).requires_grad_(True)
+        dod = hdo.to("cuda", non_blocking=True)
+        o = stk.block_sparse_attention(qd, kd, vd, mask, **kw)
+        o.backward(dod)
+        for h, d in zip(out_h, (o.detach(), qd.grad, kd.grad, vd.grad)):
+            h.copy_(d, non_blocking=True)
+
+    e_steps = max(2, min(args.steps, 5))
+    e_ms, _, _ = time_steps(dist, e2e_step, e_steps, 1)
+    del dq_, dk_, dv_
+    bytes_h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+    bytes_d2h = sum(t.numel() * t.element_size() for t in out_h)
+    e2e = {"value": round(3.5 * F * dist.world * e_steps / (e_ms / 1e3) / 1e12, 3),
+           "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d, "d2h_bytes_per_step": bytes_d2h,
+           "ms_per_step": round(e_ms / e_steps, 3)}
+    rl = roofline(per_kernel, F, pk, src, sustained=True)
+    res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
+               nnz=nnz, flops_fwd=F, finite=finite, per_kernel=per_kernel)
+    del q, k, v, do, hq, hk, hv, hdo, out_h
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_fwd(dist, args, pk, src):
+    import sparse_triton_kernel as stk
+    cfg = CFG3
+    nnz, mask = kept_blocks(cfg)
+    F = f_fwd(cfg, nnz)
+    q, k, v = make_inputs(cfg, dist.rank)
+    kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
+              window_size=cfg["W"])
+
+    def step():
+        with torch.no_grad():
+            return stk.block_sparse_attention(q, k, v, mask, **kw)
+
+    ms, launches, per_kernel = time_steps(dist, step, max(2, args.steps), args.warmup)
+    value = F * dist.world * max(2, args.steps) / (ms / 1e3) / 1e12
+    rl = roofline(per_kernel, F, pk, src, sustained=False)
+    del q, k, v
+    torch.cuda.empty_cache()
+    return dict(value=value, ms=ms / max(2, args.steps), roofline=rl, nnz=nnz, launches=launches)
+
+
+def bench_decode(dist, args, pk, src):
+    import sparse_triton_kernel as stk
+    cfg = CFG4
+    _, mask = kept_blocks(cfg)
+    q, k, v = make_inputs(cfg, dist.rank, n_q=1)
+    kv_bytes, qo_bytes = decode_bytes(cfg)
+    kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
+              window_size=cfg["W"])
+
+    def step():
+        with torch.no_grad():
+            return stk.block_sparse_attention(q, k, v, mask, **kw)
+
+    steps = max(5, args.steps * 5)
+    ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
+    value = kv_bytes * dist.world * steps / (ms / 1e3) / 1e9
+    rl = roofline(per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes)
+    del q, k, v
+    torch.cuda.empty_cache()
+    return dict(value=value, ms=ms / steps, roofline=rl, kv_bytes=kv_bytes, qo_bytes=qo_bytes,
+                launches=launches)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (upstream eager masked attention, oracle port)
+# ---------------------------------------------------------------------------
+
+
+def cpu_baseline_fwdbwd(budget_s: float = 20.0):
+    """Eager fwd+bwd of one (batch, head) slice of config 2 on the host:
+    the bottom-right 1024 query rows against all 16384 keys (fp32), repeated
+    while the budget lasts, extrapolated x16 rows x128 slices."""
+    from oracle import streaming_oracle as orc
+    cfg = CFG2
+    rows = 1024
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 1, rows, cfg["D"], generator=g)
+    k = torch.randn(1, 1, cfg["N"], cfg["D"], generator=g)
+    v = torch.randn(1, 1, cfg["N"], cfg["D"], generator=g)
+    do = torch.randn(1, 1, rows, cfg["D"], generator=g)
+    mask = orc.make_streaming_mask(rows, cfg["N"], cfg["S"], cfg["W"], cfg["BM"], cfg["BN"])
+    kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
+              window_size=cfg["W"])
+    orc.attention_forward_backward(q, k, v, do, mask, **kw)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        orc.attention_forward_backward(q, k, v, do, mask, **kw)
+        n += 1
+        if time.perf_counter() - t0 > budget_s or n >= 20:
+            break
+    per = (time.perf_counter() - t0) / n
+    full_step_s = per * (cfg["N"] / rows) * cfg["B"] * cfg["H"]
+    nnz = int(orc.make_streaming_mask(cfg["N"], cfg["N"], cfg["S"], cfg["W"], cfg["BM"],
+                                      cfg["BN"]).sum())
+    flops = 3.5 * f_fwd(cfg, nnz)
+    return {"value": round(flops / full_step_s / 1e12, 6), "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 of 128 (b,h) slices; bottom-right {rows} of {cfg['N']} query rows x "
+                      f"{cfg['N']} keys; fp32 eager fwd+bwd (torch autograd), {n} reps of "
+                      f"{per:.3f} s; extrapolated x{cfg['N'] // rows} rows x128 slices",
+            "seconds_per_full_step": round(full_step_s, 2)}
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+
+def base_line(args, world):
+    return {"metric": "kept-block attn TFLOP/s fwd+bwd", "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v/dO, BASELINE config 2 shapes)",
+            "config": {"workload": "cfg2 sparse prefill fwd+bwd: B=4 H=32 N=16384 D=128 bf16 "
+                                   "S=4 W=2048 BM=BN=128 per rank",
+                       "global_batch": 4 * world, "seq_len": 16384, "heads": 32,
+                       "head_dim": 128, "parallelism": f"(batch,head) shards x{world}",
+                       "l2": "inputs exceed L2 (537 MB per tensor); no flush"}}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    budget = max(10.0, min(60.0, 6.0 * args.steps))
+    cb = cpu_baseline_fwdbwd(budget_s=budget)
+    line = base_line(args, world)
+    line.update({"impl": "reference", "value": cb["value"],
+                 "ms_per_step": round(cb["seconds_per_full_step"] * 1e3, 1),
+                 "dtype": "f32 (host eager)", "cpu_baseline": cb,
+                 "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}, "gpu_launches": 0})
+    line["config"]["workload"] += " (host eager sample, extrapolated)"
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["all", "fwdbwd", "fwd", "decode"], default="all")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    dist = Dist(args.gpus)
+    dist.init()
+    import sbfa_native as native
+    native.lib()
+    pk, src = peaks()
+    line = base_line(args, dist.world)
+    extra = {}
+    if args.workload in ("all", "fwdbwd"):
+        r = bench_fwdbwd(dist, args, pk, src)
+        line.update({"value": round(r["value"], 3), "ms_per_step": round(r["ms"] / args.steps, 3),
+                     "e2e": r["e2e"], "roofline": r["roofline"], "clocks": r["clocks"],
+                     "gpu_launches": r["launches"]})
+        extra["fwdbwd"] = {"kept_blocks": r["nnz"], "flops_fwd": r["flops_fwd"],
+                           "outputs_finite_all_ranks": r["finite"],
+                           "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()}}
+    if args.workload in ("all", "fwd"):
+        r = bench_fwd(dist, args, pk, src)
+        extra["cfg3_prefill_fwd"] = {"value": round(r["value"], 3), "unit": "TFLOP/s",
+                                     "ms_per_step": round(r["ms"], 3), "roofline": r["roofline"],
+                                     "kept_blocks": r["nnz"], "gpu_launches": r["launches"]}
+        if args.workload == "fwd":
+            line.update({"metric": "kept-block attn TFLOP/s fwd", "value": extra[
+                "cfg3_prefill_fwd"]["value"], "roofline": r["roofline"], "dtype": "fp16"})
+    if args.workload in ("all", "decode"):
+        r = bench_decode(dist, args, pk, src)
+        extra["cfg4_decode"] = {"value": round(r["value"], 2), "unit": "GB/s",
+                                "ms_per_step": round(r["ms"], 4), "roofline": r["roofline"],
+                                "kv_bytes_per_step": r["kv_bytes"],
+                                "gpu_launches": r["launches"]}
+        if args.workload == "decode":
+            line.update({"metric": "decode KV GB/s", "unit": "GB/s", "value": extra[
+                "cfg4_decode"]["value"], "roofline": r["roofline"], "dtype": "fp16"})
+    line["extra"] = extra
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and \
+            args.workload in ("all", "fwdbwd"):
+        line["cpu_baseline"] = cpu_baseline_fwdbwd(budget_s=20.0)
+    if dist.rank == 0:
+        print(json.dumps(line))
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

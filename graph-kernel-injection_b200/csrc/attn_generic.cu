@@ -1,0 +1,517 @@
+// CUDA-core ("generic") block-sparse attention kernels.
+//
+// These cover every dtype (fp16, bf16, fp32, fp64) and head dims up to 256
+// (128 for fp64) with exact fp32 (fp64 for fp64 inputs) arithmetic.  The
+// tensor-core kernels in attn_tc.cu take the bf16/fp16 hot shapes; these
+// take everything else (the upstream fp32 verification tiers, fp64
+// gradcheck, head dims 16/32, tiny tiles).
+//
+// Semantics follow sparse_triton_kernel.py exactly:
+//   forward  :231-352  online softmax, natural exp, LSE = m + log(l), empty
+//                      rows -> O = 0, LSE = 0
+//   delta    :355-392  Delta = rowsum(O * dO) in fp32
+//   dK/dV    :395-509  P = exp(S - LSE), dV += P^T dO, dS = P (dP - Delta) s,
+//                      dK += dS^T Q
+//   dQ       :512-601  dQ += dS K
+// but each kernel walks a compacted list of kept tiles (sbfa_build_plan)
+// instead of scanning the whole mask row/column.
+//
+// Tiling: forward and dQ use 16 query rows x 64 keys per CTA step (4 warps,
+// 4 rows per warp, lanes over keys for QK^T and over head-dim for PV);
+// dK/dV uses 16 keys x 64 query rows.
+#include "sbfa_common.cuh"
+
+namespace sbfa {
+namespace {
+
+constexpr int kRows = 16;      // query rows per CTA (fwd, dQ)
+constexpr int kKeys = 64;      // keys per tile (fwd, dQ)
+constexpr int kKvKeys = 16;    // keys per CTA (dK/dV)
+constexpr int kKvRows = 64;    // query rows per tile (dK/dV)
+constexpr int kThreads = 128;
+
+template <typename A>
+__device__ __forceinline__ A warp_max(A x) {
+  for (int o = 16; o > 0; o >>= 1) x = max(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+template <typename A>
+__device__ __forceinline__ A warp_sum(A x) {
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Load `rows` rows of a [N, D] slice starting at row r0 into smem (row
+// stride `ld`), converting to the accumulator type; rows >= n are zero.
+template <typename T, typename A>
+__device__ __forceinline__ void load_rows(A* dst, int ld, const T* src, int r0, int rows,
+                                          int n, int D) {
+  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
+    int r = i / D, d = i - r * D;
+    int gr = r0 + r;
+    dst[r * ld + d] = gr < n ? Elem<T>::to(src[(size_t)gr * D + d]) : A(0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+template <typename T, int DPL>
+__global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    T* __restrict__ o, float* __restrict__ lse, int D, float scale_f, MaskParams mp,
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+  using A = typename Elem<T>::acc;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  A* Qs = reinterpret_cast<A*>(smem_raw);   // [kRows][D]
+  A* Ks = Qs + kRows * D;                   // [kKeys][D+1]
+  A* Vs = Ks + kKeys * (D + 1);             // [kKeys][D]
+  const int ti = blockIdx.x;
+  const size_t bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const A scale = (A)scale_f;
+  const T* qb = q + bh * (size_t)mp.n_q * D;
+  const T* kb = k + bh * (size_t)mp.n_kv * D;
+  const T* vb = v + bh * (size_t)mp.n_kv * D;
+  const int row0 = ti * kRows;
+  load_rows<T, A>(Qs, D, qb, row0, kRows, mp.n_q, D);
+
+  A m[4], l[4], acc[4][DPL];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    m[r] = neg_inf<A>();
+    l[r] = 0;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[r][i] = 0;
+  }
+  const int e0 = row_ptr[ti], e1 = row_ptr[ti + 1];
+  for (int e = e0; e < e1; ++e) {
+    const int32_t ent = col_idx[e];
+    const int tj = plan_index(ent);
+    const bool partial = plan_partial(ent);
+    const int k0 = tj * kKeys;
+    __syncthreads();
+    load_rows<T, A>(Ks, D + 1, kb, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Vs, D, vb, k0, kKeys, mp.n_kv, D);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int lr = warp * 4 + r;
+      const int row = row0 + lr;
+      A s0 = 0, s1 = 0;
+      const A* qr = Qs + lr * D;
+      const A* k0r = Ks + lane * (D + 1);
+      const A* k1r = Ks + (lane + 32) * (D + 1);
+      for (int d = 0; d < D; ++d) {
+        A qd = qr[d];
+        s0 += qd * k0r[d];
+        s1 += qd * k1r[d];
+      }
+      const bool v0 = visible(mp, row, k0 + lane, partial);
+      const bool v1 = visible(mp, row, k0 + lane + 32, partial);
+      s0 = v0 ? s0 * scale : neg_inf<A>();
+      s1 = v1 ? s1 * scale : neg_inf<A>();
+      const A m_new = max(m[r], warp_max(max(s0, s1)));
+      if (m_new == neg_inf<A>()) continue;  // nothing visible yet (warp-uniform)
+      const A alpha = (m[r] == neg_inf<A>()) ? A(0) : acc_exp<A>(m[r] - m_new);
+      const A p0 = v0 ? acc_exp<A>(s0 - m_new) : A(0);
+      const A p1 = v1 ? acc_exp<A>(s1 - m_new) : A(0);
+      l[r] = l[r] * alpha + warp_sum(p0 + p1);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[r][i] *= alpha;
+      for (int j = 0; j < 32; ++j) {
+        const A pj0 = __shfl_sync(0xffffffffu, p0, j);
+        const A pj1 = __shfl_sync(0xffffffffu, p1, j);
+        const A* va = Vs + j * D;
+        const A* vc = Vs + (j + 32) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) acc[r][i] += pj0 * va[d] + pj1 * vc[d];
+        }
+      }
+      m[r] = m_new;
+    }
+  }
+  T* ob = o + bh * (size_t)mp.n_q * D;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = row0 + warp * 4 + r;
+    if (row >= mp.n_q) continue;
+    const bool valid = l[r] > A(0);
+    const A inv = valid ? A(1) / l[r] : A(1);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) ob[(size_t)row * D + d] = Elem<T>::from(valid ? acc[r][i] * inv : A(0));
+    }
+    if (lane == 0)
+      lse[bh * mp.n_q + row] = valid ? (float)(m[r] + acc_log<A>(l[r])) : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward: Delta = rowsum(O * dO)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+                             float* __restrict__ delta, int64_t rows, int D) {
+  using A = typename Elem<T>::acc;
+  const int lane = threadIdx.x & 31;
+  int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (; r < rows; r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    A s = 0;
+    for (int d = lane; d < D; d += 32)
+      s += Elem<T>::to(o[r * D + d]) * Elem<T>::to(dout[r * D + d]);
+    s = warp_sum(s);
+    if (lane == 0) delta[r] = (float)s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward: dQ
+// ---------------------------------------------------------------------------
+template <typename T, int DPL>
+__global__ void __launch_bounds__(kThreads) dq_generic_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const T* __restrict__ dout, const float* __restrict__ lse,
+    const float* __restrict__ delta, T* __restrict__ dq, int D, float scale_f, MaskParams mp,
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+  using A = typename Elem<T>::acc;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  A* Qs = reinterpret_cast<A*>(smem_raw);   // [kRows][D]
+  A* dOs = Qs + kRows * D;                  // [kRows][D]
+  A* Ks = dOs + kRows * D;                  // [kKeys][D+1]
+  A* Vs = Ks + kKeys * (D + 1);             // [kKeys][D+1]
+  const int ti = blockIdx.x;
+  const size_t bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const A scale = (A)scale_f;
+  const T* kb = k + bh * (size_t)mp.n_kv * D;
+  const T* vb = v + bh * (size_t)mp.n_kv * D;
+  const int row0 = ti * kRows;
+  load_rows<T, A>(Qs, D, q + bh * (size_t)mp.n_q * D, row0, kRows, mp.n_q, D);
+  load_rows<T, A>(dOs, D, dout + bh * (size_t)mp.n_q * D, row0, kRows, mp.n_q, D);
+  A lse_r[4], del_r[4], acc[4][DPL];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = row0 + warp * 4 + r;
+    lse_r[r] = row < mp.n_q ? (A)lse[bh * mp.n_q + row] : A(0);
+    del_r[r] = row < mp.n_q ? (A)delta[bh * mp.n_q + row] : A(0);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[r][i] = 0;
+  }
+  const int e0 = row_ptr[ti], e1 = row_ptr[ti + 1];
+  for (int e = e0; e < e1; ++e) {
+    const int32_t ent = col_idx[e];
+    const int tj = plan_index(ent);
+    const bool partial = plan_partial(ent);
+    const int k0 = tj * kKeys;
+    __syncthreads();
+    load_rows<T, A>(Ks, D + 1, kb, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Vs, D + 1, vb, k0, kKeys, mp.n_kv, D);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int lr = warp * 4 + r;
+      const int row = row0 + lr;
+      const A* qr = Qs + lr * D;
+      const A* dor = dOs + lr * D;
+      A s0 = 0, s1 = 0, dp0 = 0, dp1 = 0;
+      const A* k0r = Ks + lane * (D + 1);
+      const A* k1r = Ks + (lane + 32) * (D + 1);
+      const A* v0r = Vs + lane * (D + 1);
+      const A* v1r = Vs + (lane + 32) * (D + 1);
+      for (int d = 0; d < D; ++d) {
+        const A qd = qr[d], gd = dor[d];
+        s0 += qd * k0r[d];
+        s1 += qd * k1r[d];
+        dp0 += gd * v0r[d];
+        dp1 += gd * v1r[d];
+      }
+      const bool vis0 = visible(mp, row, k0 + lane, partial);
+      const bool vis1 = visible(mp, row, k0 + lane + 32, partial);
+      const A p0 = vis0 ? acc_exp<A>(s0 * scale - lse_r[r]) : A(0);
+      const A p1 = vis1 ? acc_exp<A>(s1 * scale - lse_r[r]) : A(0);
+      const A ds0 = p0 * (dp0 - del_r[r]) * scale;
+      const A ds1 = p1 * (dp1 - del_r[r]) * scale;
+      for (int j = 0; j < 32; ++j) {
+        const A a0 = __shfl_sync(0xffffffffu, ds0, j);
+        const A a1 = __shfl_sync(0xffffffffu, ds1, j);
+        const A* ka = Ks + j * (D + 1);
+        const A* kc = Ks + (j + 32) * (D + 1);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) acc[r][i] += a0 * ka[d] + a1 * kc[d];
+        }
+      }
+    }
+  }
+  T* dqb = dq + bh * (size_t)mp.n_q * D;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = row0 + warp * 4 + r;
+    if (row >= mp.n_q) continue;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) dqb[(size_t)row * D + d] = Elem<T>::from(acc[r][i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward: dK, dV
+// ---------------------------------------------------------------------------
+template <typename T, int DPL>
+__global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const T* __restrict__ dout, const float* __restrict__ lse,
+    const float* __restrict__ delta, T* __restrict__ dk, T* __restrict__ dv, int D,
+    float scale_f, MaskParams mp, const int32_t* __restrict__ col_ptr,
+    const int32_t* __restrict__ row_idx) {
+  using A = typename Elem<T>::acc;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  A* Ks = reinterpret_cast<A*>(smem_raw);   // [kKvKeys][D]
+  A* Vs = Ks + kKvKeys * D;                 // [kKvKeys][D]
+  A* Qs = Vs + kKvKeys * D;                 // [kKvRows][D+1]
+  A* dOs = Qs + kKvRows * (D + 1);          // [kKvRows][D+1]
+  A* Ls = dOs + kKvRows * (D + 1);          // [kKvRows]
+  A* Dl = Ls + kKvRows;                     // [kKvRows]
+  const int tj = blockIdx.x;
+  const size_t bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const A scale = (A)scale_f;
+  const T* qb = q + bh * (size_t)mp.n_q * D;
+  const T* gb = dout + bh * (size_t)mp.n_q * D;
+  const int key0 = tj * kKvKeys;
+  load_rows<T, A>(Ks, D, k + bh * (size_t)mp.n_kv * D, key0, kKvKeys, mp.n_kv, D);
+  load_rows<T, A>(Vs, D, v + bh * (size_t)mp.n_kv * D, key0, kKvKeys, mp.n_kv, D);
+  A adk[4][DPL], adv[4][DPL];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) adk[c][i] = adv[c][i] = 0;
+  const int e0 = col_ptr[tj], e1 = col_ptr[tj + 1];
+  for (int e = e0; e < e1; ++e) {
+    const int32_t ent = row_idx[e];
+    const int ti = plan_index(ent);
+    const bool partial = plan_partial(ent);
+    const int r0 = ti * kKvRows;
+    __syncthreads();
+    load_rows<T, A>(Qs, D + 1, qb, r0, kKvRows, mp.n_q, D);
+    load_rows<T, A>(dOs, D + 1, gb, r0, kKvRows, mp.n_q, D);
+    for (int i = threadIdx.x; i < kKvRows; i += blockDim.x) {
+      const int row = r0 + i;
+      Ls[i] = row < mp.n_q ? (A)lse[bh * mp.n_q + row] : A(0);
+      Dl[i] = row < mp.n_q ? (A)delta[bh * mp.n_q + row] : A(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int lk = warp * 4 + c;
+      const int key = key0 + lk;
+      const A* kr = Ks + lk * D;
+      const A* vr = Vs + lk * D;
+      const A* q0r = Qs + lane * (D + 1);
+      const A* q1r = Qs + (lane + 32) * (D + 1);
+      const A* g0r = dOs + lane * (D + 1);
+      const A* g1r = dOs + (lane + 32) * (D + 1);
+      A s0 = 0, s1 = 0, dp0 = 0, dp1 = 0;
+      for (int d = 0; d < D; ++d) {
+        const A kd = kr[d], vd = vr[d];
+        s0 += q0r[d] * kd;
+        s1 += q1r[d] * kd;
+        dp0 += g0r[d] * vd;
+        dp1 += g1r[d] * vd;
+      }
+      const bool vis0 = visible(mp, r0 + lane, key, partial);
+      const bool vis1 = visible(mp, r0 + lane + 32, key, partial);
+      const A p0 = vis0 ? acc_exp<A>(s0 * scale - Ls[lane]) : A(0);
+      const A p1 = vis1 ? acc_exp<A>(s1 * scale - Ls[lane + 32]) : A(0);
+      const A ds0 = p0 * (dp0 - Dl[lane]) * scale;
+      const A ds1 = p1 * (dp1 - Dl[lane + 32]) * scale;
+      for (int j = 0; j < 32; ++j) {
+        const A pa = __shfl_sync(0xffffffffu, p0, j);
+        const A pb = __shfl_sync(0xffffffffu, p1, j);
+        const A sa = __shfl_sync(0xffffffffu, ds0, j);
+        const A sb = __shfl_sync(0xffffffffu, ds1, j);
+        const A* ga = dOs + j * (D + 1);
+        const A* gc = dOs + (j + 32) * (D + 1);
+        const A* qa = Qs + j * (D + 1);
+        const A* qc = Qs + (j + 32) * (D + 1);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) {
+            adv[c][i] += pa * ga[d] + pb * gc[d];
+            adk[c][i] += sa * qa[d] + sb * qc[d];
+          }
+        }
+      }
+    }
+  }
+  T* dkb = dk + bh * (size_t)mp.n_kv * D;
+  T* dvb = dv + bh * (size_t)mp.n_kv * D;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int key = key0 + warp * 4 + c;
+    if (key >= mp.n_kv) continue;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) {
+        dkb[(size_t)key * D + d] = Elem<T>::from(adk[c][i]);
+        dvb[(size_t)key * D + d] = Elem<T>::from(adv[c][i]);
+      }
+    }
+  }
+}
+
+template <typename T>
+size_t fwd_smem(int D) {
+  return sizeof(typename Elem<T>::acc) * ((size_t)kRows * D + kKeys * (D + 1) + kKeys * D);
+}
+template <typename T>
+size_t dq_smem(int D) {
+  return sizeof(typename Elem<T>::acc) * (2 * (size_t)kRows * D + 2 * kKeys * (D + 1));
+}
+template <typename T>
+size_t dkdv_smem(int D) {
+  return sizeof(typename Elem<T>::acc) *
+         (2 * (size_t)kKvKeys * D + 2 * kKvRows * (D + 1) + 2 * kKvRows);
+}
+
+template <typename K>
+int set_smem(K kernel, size_t bytes) {
+  return check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bytes),
+                    "cudaFuncSetAttribute(generic)");
+}
+
+template <typename T, int DPL>
+int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH,
+               int D, float scale, const MaskParams& mp, const int32_t* row_ptr,
+               const int32_t* col_idx, cudaStream_t s) {
+  auto kern = fwd_generic_kernel<T, DPL>;
+  size_t sm = fwd_smem<T>(D);
+  if (int rc = set_smem(kern, sm)) return rc;
+  dim3 grid(ceil_div_i(mp.n_q, kRows), BH);
+  {
+    LaunchScope ls("fwd_generic_kernel", s);
+    kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, D,
+                                    scale, mp, row_ptr, col_idx);
+  }
+  return check_launch("fwd_generic_kernel");
+}
+
+template <typename T, int DPL>
+int launch_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+               const void* dout, void* dq, void* dk, void* dv, float* delta, int BH, int D,
+               float scale, const MaskParams& mp, const int32_t* dq_row_ptr,
+               const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
+               const int32_t* kv_row_idx, cudaStream_t s) {
+  const int64_t rows = (int64_t)BH * mp.n_q;
+  int dgrid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 64);
+  {
+    LaunchScope ls("delta_kernel", s);
+    delta_kernel<T><<<dgrid, 256, 0, s>>>((const T*)o, (const T*)dout, delta, rows, D);
+  }
+  if (int rc = check_launch("delta_kernel")) return rc;
+  {
+    auto kern = dkdv_generic_kernel<T, DPL>;
+    size_t sm = dkdv_smem<T>(D);
+    if (int rc = set_smem(kern, sm)) return rc;
+    dim3 grid(ceil_div_i(mp.n_kv, kKvKeys), BH);
+    {
+      LaunchScope ls("dkdv_generic_kernel", s);
+      kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
+                                      lse, delta, (T*)dk, (T*)dv, D, scale, mp, kv_col_ptr,
+                                      kv_row_idx);
+    }
+    if (int rc = check_launch("dkdv_generic_kernel")) return rc;
+  }
+  {
+    auto kern = dq_generic_kernel<T, DPL>;
+    size_t sm = dq_smem<T>(D);
+    if (int rc = set_smem(kern, sm)) return rc;
+    dim3 grid(ceil_div_i(mp.n_q, kRows), BH);
+    {
+      LaunchScope ls("dq_generic_kernel", s);
+      kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
+                                      lse, delta, (T*)dq, D, scale, mp, dq_row_ptr, dq_col_idx);
+    }
+    return check_launch("dq_generic_kernel");
+  }
+}
+
+template <typename T>
+int dispatch_fwd(int D, const void* q, const void* k, const void* v, void* o, float* lse,
+                 int BH, float scale, const MaskParams& mp, const int32_t* rp,
+                 const int32_t* ci, cudaStream_t s) {
+  if (D <= 32) return launch_fwd<T, 1>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
+  if (D <= 64) return launch_fwd<T, 2>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
+  if (D <= 128) return launch_fwd<T, 4>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
+  return launch_fwd<T, 8>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
+}
+
+template <typename T>
+int dispatch_bwd(int D, const void* q, const void* k, const void* v, const void* o,
+                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
+                 int BH, float scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
+                 const int32_t* c, const int32_t* d, cudaStream_t s) {
+  if (D <= 32)
+    return launch_bwd<T, 1>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+  if (D <= 64)
+    return launch_bwd<T, 2>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+  if (D <= 128)
+    return launch_bwd<T, 4>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+  return launch_bwd<T, 8>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+}
+
+}  // namespace
+
+// Entry points used by capi.cu.
+int generic_tiles(int pass, int64_t* tm, int64_t* tn) {
+  if (pass == 2) { *tm = kKvRows; *tn = kKvKeys; }
+  else { *tm = kRows; *tn = kKeys; }
+  return SBFA_OK;
+}
+
+bool generic_supports(int dtype, int64_t D) {
+  if (D <= 0) return false;
+  if (dtype == SBFA_F64) return D <= 128;
+  return D <= 256;
+}
+
+int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o,
+                float* lse, int BH, float scale, const MaskParams& mp, const int32_t* rp,
+                const int32_t* ci, cudaStream_t s) {
+  switch (dtype) {
+    case SBFA_F16: return dispatch_fwd<__half>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
+    case SBFA_BF16: return dispatch_fwd<__nv_bfloat16>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
+    case SBFA_F32: return dispatch_fwd<float>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
+    case SBFA_F64: return dispatch_fwd<double>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
+  }
+  return fail(SBFA_ERR_INVALID, "unknown dtype");
+}
+
+int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
+                const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
+                int BH, float scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
+                const int32_t* c, const int32_t* d, cudaStream_t s) {
+  switch (dtype) {
+    case SBFA_F16:
+      return dispatch_bwd<__half>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+    case SBFA_BF16:
+      return dispatch_bwd<__nv_bfloat16>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+    case SBFA_F32:
+      return dispatch_bwd<float>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+    case SBFA_F64:
+      return dispatch_bwd<double>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+  }
+  return fail(SBFA_ERR_INVALID, "unknown dtype");
+}
+
+}  // namespace sbfa

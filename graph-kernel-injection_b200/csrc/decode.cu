@@ -1,0 +1,284 @@
+// Split-KV decode for a single query per (batch, head).
+//
+// Upstream has no decode kernel: benchmark.py:799-804 clamps block_m to 1
+// and runs the prefill _fwd_kernel (sparse_triton_kernel.py:231-352) with
+// N_Q = 1, which scans all ceil(N_KV/BN) mask entries per (b, h).  Here:
+//
+//  * the kept key tiles of mask row 0 come from a compacted plan (pass 3,
+//    64-key tiles), so only kept tiles are touched;
+//  * inside a kept tile, a key is loaded only if the query can see it
+//    (bounds, lifted block mask on partial tiles, StreamingLLM token rule),
+//    so HBM traffic is exactly the visible K/V rows;
+//  * each key row is read by a group of G lanes with 16-byte loads
+//    (G = D * sizeof(T) / 16; 16 lanes for D = 128 fp16), fully coalesced,
+//    U keys in flight per group;
+//  * every CTA keeps an online-softmax partial (m, l, acc[D]) per lane group,
+//    merges its groups through shared memory and either writes O / LSE
+//    directly (one split) or a partial to the workspace, merged by
+//    decode_merge_kernel (several splits).
+#include <algorithm>
+
+#include "sbfa_common.cuh"
+
+namespace sbfa {
+namespace {
+
+constexpr int kDecThreads = 128;
+constexpr int kDecTile = 64;   // keys per plan tile (pass 3)
+constexpr int kUnroll = 4;     // keys in flight per lane group
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& w, float* f) {
+  if constexpr (sizeof(T) == 2) {
+    const T* h = reinterpret_cast<const T*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to(h[i]);
+  } else {
+    const float* x = reinterpret_cast<const float*>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = x[i];
+  }
+}
+
+// Partial record layout in the workspace: [m, l, acc[0..D)] floats.
+template <typename T, int G>
+__global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    T* __restrict__ o, float* __restrict__ lse, float* __restrict__ ws, int D, float scale,
+    MaskParams mp, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+    int nsplit) {
+  constexpr int EPV = 16 / sizeof(T);      // elements per 16-byte vector
+  constexpr int GPW = 32 / G;              // lane groups per warp
+  constexpr int NG = (kDecThreads / 32) * GPW;
+  __shared__ float sm_m[NG], sm_l[NG];
+  extern __shared__ float sm_acc[];        // [NG][D]
+
+  const int split = blockIdx.x;
+  const size_t bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane / G, gl = lane % G;
+  const int gid = warp * GPW + grp;
+
+  // query slice of this lane, pre-scaled
+  float qv[EPV];
+  {
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(q + bh * (size_t)D) + gl);
+    unpack16<T>(w, qv);
+#pragma unroll
+    for (int i = 0; i < EPV; ++i) qv[i] *= scale;
+  }
+  const int n_tiles = row_ptr[1] - row_ptr[0];
+  const int per = (n_tiles + nsplit - 1) / nsplit;
+  const int t0 = row_ptr[0] + split * per;
+  const int t1 = min(row_ptr[0] + n_tiles, t0 + per);
+  const int total = max(0, t1 - t0) * kDecTile;
+  const uint4* kb = reinterpret_cast<const uint4*>(k + bh * (size_t)mp.n_kv * D);
+  const uint4* vb = reinterpret_cast<const uint4*>(v + bh * (size_t)mp.n_kv * D);
+  const int vec_per_row = D / EPV;   // == G
+
+  float m = -INFINITY, l = 0.f, acc[EPV];
+#pragma unroll
+  for (int i = 0; i < EPV; ++i) acc[i] = 0.f;
+
+  const int step = NG * kUnroll;
+  for (int base = 0; base < total; base += step) {
+    uint4 kw[kUnroll], vw[kUnroll];
+    bool vis[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = base + u * NG + gid;
+      vis[u] = false;
+      if (t < total) {
+        const int32_t ent = col_idx[t0 + t / kDecTile];
+        const int key = plan_index(ent) * kDecTile + (t % kDecTile);
+        vis[u] = visible(mp, 0, key, plan_partial(ent));
+        if (vis[u]) {
+          kw[u] = __ldg(kb + (size_t)key * vec_per_row + gl);
+          vw[u] = __ldg(vb + (size_t)key * vec_per_row + gl);
+        }
+      }
+    }
+    float s[kUnroll];
+    float tile_max = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      float kf[EPV];
+      float d = 0.f;
+      if (vis[u]) {
+        unpack16<T>(kw[u], kf);
+#pragma unroll
+        for (int i = 0; i < EPV; ++i) d += qv[i] * kf[i];
+      }
+#pragma unroll
+      for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      s[u] = vis[u] ? d : -INFINITY;
+      tile_max = fmaxf(tile_max, s[u]);
+    }
+    // No shuffles below this point in the iteration, so the per-group
+    // branch cannot split a warp-collective.
+    const float m_new = fmaxf(m, tile_max);
+    if (m_new != -INFINITY) {
+      const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
+      l *= alpha;
+#pragma unroll
+      for (int i = 0; i < EPV; ++i) acc[i] *= alpha;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (!vis[u]) continue;
+        const float p = __expf(s[u] - m_new);
+        l += p;
+        float vf[EPV];
+        unpack16<T>(vw[u], vf);
+#pragma unroll
+        for (int i = 0; i < EPV; ++i) acc[i] += p * vf[i];
+      }
+      m = m_new;
+    }
+  }
+
+  // merge lane groups of the CTA
+  if (gl == 0) { sm_m[gid] = m; sm_l[gid] = l; }
+#pragma unroll
+  for (int i = 0; i < EPV; ++i) sm_acc[gid * D + gl * EPV + i] = acc[i];
+  __syncthreads();
+  float M = -INFINITY;
+  for (int g = 0; g < NG; ++g) M = fmaxf(M, sm_m[g]);
+  float L = 0.f;
+  for (int g = 0; g < NG; ++g)
+    if (sm_m[g] != -INFINITY) L += sm_l[g] * __expf(sm_m[g] - M);
+  if (nsplit == 1) {
+    const bool valid = L > 0.f;
+    const float inv = valid ? 1.f / L : 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+      if (valid)
+        for (int g = 0; g < NG; ++g)
+          if (sm_m[g] != -INFINITY) a += sm_acc[g * D + d] * __expf(sm_m[g] - M);
+      o[bh * D + d] = Elem<T>::from(a * inv);
+    }
+    if (threadIdx.x == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
+  } else {
+    float* rec = ws + (bh * nsplit + split) * (size_t)(D + 2);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+      for (int g = 0; g < NG; ++g)
+        if (sm_m[g] != -INFINITY) a += sm_acc[g * D + d] * __expf(sm_m[g] - M);
+      rec[2 + d] = a;
+    }
+    if (threadIdx.x == 0) { rec[0] = M; rec[1] = L; }
+  }
+}
+
+template <typename T>
+__global__ void decode_merge_kernel(const float* __restrict__ ws, T* __restrict__ o,
+                                    float* __restrict__ lse, int D, int nsplit) {
+  const size_t bh = blockIdx.x;
+  const float* recs = ws + bh * nsplit * (size_t)(D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, recs[s * (D + 2)]);
+  float L = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float ms = recs[s * (D + 2)];
+    if (ms != -INFINITY) L += recs[s * (D + 2) + 1] * __expf(ms - M);
+  }
+  const bool valid = L > 0.f;
+  const float inv = valid ? 1.f / L : 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float a = 0.f;
+    if (valid)
+      for (int s = 0; s < nsplit; ++s) {
+        const float ms = recs[s * (D + 2)];
+        if (ms != -INFINITY) a += recs[s * (D + 2) + 2 + d] * __expf(ms - M);
+      }
+    o[bh * D + d] = Elem<T>::from(a * inv);
+  }
+  if (threadIdx.x == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
+}
+
+template <typename T, int G>
+int launch_decode(const void* q, const void* k, const void* v, void* o, float* lse, float* ws,
+                  int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
+                  const int32_t* ci, int nsplit, cudaStream_t s) {
+  constexpr int NG = (kDecThreads / 32) * (32 / G);
+  const size_t sm = sizeof(float) * NG * D;
+  auto kern = decode_split_kernel<T, G>;
+  if (sm > 48 * 1024) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)sm), "cudaFuncSetAttribute(decode)"))
+      return rc;
+  }
+  dim3 grid(nsplit, BH);
+  {
+    LaunchScope ls("decode_split_kernel", s);
+    kern<<<grid, kDecThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, ws,
+                                       D, scale, mp, rp, ci, nsplit);
+  }
+  if (int rc = check_launch("decode_split_kernel")) return rc;
+  if (nsplit > 1) {
+    {
+      LaunchScope ls("decode_merge_kernel", s);
+      decode_merge_kernel<T><<<BH, 128, 0, s>>>(ws, (T*)o, lse, D, nsplit);
+    }
+    return check_launch("decode_merge_kernel");
+  }
+  return SBFA_OK;
+}
+
+template <typename T>
+int dispatch_decode(int G, const void* q, const void* k, const void* v, void* o, float* lse,
+                    float* ws, int BH, int D, float scale, const MaskParams& mp,
+                    const int32_t* rp, const int32_t* ci, int nsplit, cudaStream_t s) {
+  switch (G) {
+    case 1: return launch_decode<T, 1>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 2: return launch_decode<T, 2>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 4: return launch_decode<T, 4>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 8: return launch_decode<T, 8>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 16: return launch_decode<T, 16>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 32: return launch_decode<T, 32>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+  }
+  return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported head_dim for the vector layout");
+}
+
+}  // namespace
+
+int decode_tile() { return kDecTile; }
+
+// Lanes per key row, or 0 when the head dim does not map onto 16-byte
+// vectors (the caller then uses the generic forward).
+int decode_group(int dtype, int64_t D) {
+  int es = (dtype == SBFA_F32) ? 4 : (dtype == SBFA_F64 ? 8 : 2);
+  if (dtype == SBFA_F64) return 0;
+  int64_t bytes = D * es;
+  if (bytes % 16 != 0) return 0;
+  int64_t g = bytes / 16;
+  if (g == 1 || g == 2 || g == 4 || g == 8 || g == 16 || g == 32) return (int)g;
+  return 0;
+}
+
+// Number of splits per (b, h): enough CTAs for ~16 per SM, never more than
+// the tiles a row can hold.
+int decode_nsplit(int64_t BH, int64_t est_tiles) {
+  int64_t target = 148 * 16;
+  int64_t ns = (target + BH - 1) / BH;
+  ns = std::max<int64_t>(1, std::min<int64_t>(ns, std::max<int64_t>(1, est_tiles)));
+  return (int)std::min<int64_t>(ns, 64);
+}
+
+int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit) {
+  return nsplit <= 1 ? 0 : BH * nsplit * (D + 2) * (int64_t)sizeof(float);
+}
+
+int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
+               void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
+               const int32_t* ci, int nsplit, cudaStream_t s) {
+  const int G = decode_group(dtype, D);
+  float* w = (float*)ws;
+  switch (dtype) {
+    case SBFA_F16: return dispatch_decode<__half>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
+    case SBFA_BF16: return dispatch_decode<__nv_bfloat16>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
+    case SBFA_F32: return dispatch_decode<float>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
+  }
+  return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported dtype");
+}
+
+}  // namespace sbfa

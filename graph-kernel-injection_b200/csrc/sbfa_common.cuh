@@ -1,0 +1,128 @@
+// Shared device/host helpers for libsbfa: element types, the StreamingLLM
+// token rule, the per-device status word and host-side error reporting.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/sbfa.h"
+
+namespace sbfa {
+
+// ---------------------------------------------------------------------------
+// Element types
+// ---------------------------------------------------------------------------
+
+template <typename T> struct Elem;
+template <> struct Elem<__half> {
+  using acc = float;
+  static __device__ __forceinline__ float to(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from(float x) { return __float2half_rn(x); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  using acc = float;
+  static __device__ __forceinline__ float to(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
+};
+template <> struct Elem<float> {
+  using acc = float;
+  static __device__ __forceinline__ float to(float x) { return x; }
+  static __device__ __forceinline__ float from(float x) { return x; }
+};
+template <> struct Elem<double> {
+  using acc = double;
+  static __device__ __forceinline__ double to(double x) { return x; }
+  static __device__ __forceinline__ double from(double x) { return x; }
+};
+
+template <typename A> __device__ __forceinline__ A acc_exp(A x);
+template <> __device__ __forceinline__ float acc_exp<float>(float x) { return expf(x); }
+template <> __device__ __forceinline__ double acc_exp<double>(double x) { return exp(x); }
+template <typename A> __device__ __forceinline__ A acc_log(A x);
+template <> __device__ __forceinline__ float acc_log<float>(float x) { return logf(x); }
+template <> __device__ __forceinline__ double acc_log<double>(double x) { return log(x); }
+template <typename A> __device__ __forceinline__ A neg_inf();
+template <> __device__ __forceinline__ float neg_inf<float>() { return -INFINITY; }
+template <> __device__ __forceinline__ double neg_inf<double>() { return -(double)INFINITY; }
+
+// ---------------------------------------------------------------------------
+// Mask semantics (one place, used by every kernel)
+// ---------------------------------------------------------------------------
+
+// Per-call mask parameters.  sink/window are pre-clamped on the host to
+// [0, n_kv] / [0, n_kv + 1] so every position fits in int32 and the rule is
+// unchanged (a window longer than q + 1 already admits every k <= q).
+struct MaskParams {
+  const int32_t* block_mask;  // [n_qb, n_kb] int32
+  int n_q, n_kv;
+  int q_off;                  // n_kv - n_q
+  int block_m, block_n, n_kb;
+  int sink, window;
+  int causal;
+};
+
+// Token rule of sparse_triton_kernel.py:315-319 at absolute positions.
+__device__ __forceinline__ bool token_visible(int qpos, int k, int sink, int window) {
+  return (k <= qpos) && (k < sink || k >= qpos - window + 1);
+}
+
+// Lifted block-mask entry for (query row, key) (sparse_triton_kernel.py:877-879).
+__device__ __forceinline__ bool lifted_visible(const MaskParams& mp, int row, int k) {
+  return __ldg(mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb + (k / mp.block_n)) != 0;
+}
+
+// Full visibility of element (row, k): bounds, lifted block mask (only when
+// the tile is partial), token rule (only when causal).
+__device__ __forceinline__ bool visible(const MaskParams& mp, int row, int k, bool partial) {
+  if (row >= mp.n_q || k >= mp.n_kv) return false;
+  if (partial && !lifted_visible(mp, row, k)) return false;
+  if (mp.causal && !token_visible(mp.q_off + row, k, mp.sink, mp.window)) return false;
+  return true;
+}
+
+constexpr uint32_t kPartialBit = 0x80000000u;
+__device__ __forceinline__ int plan_index(int32_t e) { return (int)((uint32_t)e & ~kPartialBit); }
+__device__ __forceinline__ bool plan_partial(int32_t e) { return ((uint32_t)e & kPartialBit) != 0; }
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing
+// ---------------------------------------------------------------------------
+
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int check_cuda(cudaError_t e, const char* what);
+int check_launch(const char* what);
+
+// Device address of the status word of the current device (allocated once
+// per device inside libsbfa, zero-initialised).
+int* device_status_ptr();
+
+// Status codes a kernel may record (first writer wins).
+constexpr int kStatusWaitTimeout = 1;
+__device__ __forceinline__ void record_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+inline int ceil_div_i(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// Wraps one kernel launch: counts it, and when timing is enabled
+// (sbfa_timing_enable) records a CUDA event pair around it on its stream,
+// tagged with `name`, for sbfa_timing_read.
+class LaunchScope {
+ public:
+  LaunchScope(const char* name, cudaStream_t s);
+  ~LaunchScope();
+  LaunchScope(const LaunchScope&) = delete;
+  LaunchScope& operator=(const LaunchScope&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t stream_;
+  cudaEvent_t start_ = nullptr;
+};
+
+}  // namespace sbfa

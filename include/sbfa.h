@@ -1,0 +1,175 @@
+/*
+ * sbfa.h - C ABI of libsbfa.so, the B200 (sm_100a) kernels for StreamingLLM
+ * sink+window block-sparse attention.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor pointers are DEVICE pointers on the current CUDA device.
+ *   - Q/K/V/O/dO/dQ/dK/dV are contiguous [B, H, N, D] row-major; LSE and
+ *     Delta are contiguous fp32 [B, H, N_Q].  (The upstream Python bridge
+ *     forces .contiguous() on its inputs, sparse_triton_kernel.py:834,707.)
+ *   - `stream` is a cudaStream_t passed as void*; every launch is
+ *     asynchronous on it.  NULL means the legacy default stream.
+ *   - Return value: SBFA_OK (0) or an SBFA_ERR_* code; sbfa_last_error()
+ *     gives the message of the last failure on the calling thread.
+ *   - Block masks are int32 [ceil(n_q/block_m), ceil(n_kv/block_n)], nonzero
+ *     = keep, shared by every (batch, head) exactly as upstream
+ *     (sparse_triton_kernel.py:645-650).
+ *   - Queries are bottom-right aligned: query row r sits at absolute
+ *     position (n_kv - n_q) + r (sparse_triton_kernel.py:655-660).
+ *   - With is_causal != 0 a kept block additionally applies the token rule
+ *     visible(q,k) = (k <= q) && (k < sink || k >= q - window + 1)
+ *     (sparse_triton_kernel.py:315-322); with is_causal == 0 only the block
+ *     mask (and sequence bounds) apply.
+ *   - A query row with no visible key produces O = 0 and LSE = 0
+ *     (sparse_triton_kernel.py:341-352) and zero gradients.
+ */
+#ifndef SBFA_H_
+#define SBFA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum sbfa_status {
+  SBFA_OK = 0,
+  SBFA_ERR_INVALID = 1,     /* bad argument (shape, pointer, size) */
+  SBFA_ERR_UNSUPPORTED = 2, /* valid request this build has no kernel for */
+  SBFA_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  SBFA_ERR_DEVICE = 4       /* a kernel reported a failure through the status word */
+};
+
+enum sbfa_dtype { SBFA_F16 = 0, SBFA_BF16 = 1, SBFA_F32 = 2, SBFA_F64 = 3 };
+
+/* ABI version of this header (bumped on any signature change). */
+int sbfa_abi_version(void);
+
+/* Copy the calling thread's last error message (NUL-terminated, truncated to
+ * len) into buf.  Returns the full message length. */
+int sbfa_last_error(char* buf, size_t len);
+
+/* Read and clear the device status word of the current device (a blocking
+ * device->host read of 4 bytes).  0 = no kernel reported a failure since
+ * the last call; otherwise the first failure code a kernel recorded
+ * (1 = a bounded wait on a pipeline barrier expired). */
+int sbfa_device_status(int* status_out);
+
+/* Total kernel launches issued by this library in this process. */
+int64_t sbfa_launch_count(void);
+
+/* Per-kernel device timing (no upstream counterpart; upstream times whole
+ * calls with torch.cuda.Event, benchmark.py:438-492).  While enabled, every
+ * launch records a CUDA event pair around itself on its own stream.
+ * sbfa_timing_read waits for the recorded events, writes up to max_kernels
+ * aggregated rows (name as a NUL-terminated string in a 64-byte slot of
+ * names, summed milliseconds, launch count), returns the row count through
+ * n_out and clears the record. */
+int sbfa_timing_enable(int on);
+int sbfa_timing_read(int max_kernels, char* names, double* total_ms, int64_t* launches,
+                     int* n_out);
+
+/* ---------------------------------------------------------------------------
+ * Masks and plans
+ * ------------------------------------------------------------------------- */
+
+/* Dense int32 block mask, bit-exact with make_streaming_mask
+ * (sparse_triton_kernel.py:104-181): entry (i, j) is
+ *   (q_hi > k_lo) & ((k_lo < sink) | (k_hi - 1 >= q_lo - window + 1))
+ * with q_lo = i*block_m + (n_kv - n_q), q_hi = q_lo + block_m,
+ * k_lo = j*block_n, k_hi = k_lo + block_n (unclamped).
+ * mask_out: int32[ceil(n_q/block_m) * ceil(n_kv/block_n)]. */
+int sbfa_streaming_mask(int64_t n_q, int64_t n_kv, int64_t sink, int64_t window,
+                        int64_t block_m, int64_t block_n, int32_t* mask_out,
+                        void* stream);
+
+/* Dense (causal=0) or dense-causal block mask, bit-exact with
+ * make_dense_mask (sparse_triton_kernel.py:184-210). */
+int sbfa_dense_mask(int64_t n_q, int64_t n_kv, int64_t block_m, int64_t block_n,
+                    int causal, int32_t* mask_out, void* stream);
+
+/* Compacted kept-tile lists of a block mask re-tiled to (tile_m, tile_n).
+ * Replaces the per-iteration mask scans of the upstream kernels
+ * (sparse_triton_kernel.py:283-285, 448-449, 563-565).
+ * Tile (I, J) covers rows [I*tile_m, (I+1)*tile_m) and keys
+ * [J*tile_n, (J+1)*tile_n), clipped to n_q / n_kv; it is kept iff any user
+ * block it overlaps is nonzero.  Index entries carry bit 31 set when some
+ * overlapped user block is zero ("partial" tile: the kernel must test the
+ * lifted block mask per element).
+ *   row_ptr: int32[n_ti + 1], col_idx: int32[n_ti * n_tj]   (CSR, by query tile)
+ *   col_ptr: int32[n_tj + 1], row_idx: int32[n_ti * n_tj]   (CSC, by key tile)
+ *   nnz_out: int32[1] (device), number of kept tiles.
+ * Any of the CSR / CSC pairs may be NULL to skip it. */
+int sbfa_build_plan(const int32_t* block_mask, int64_t n_q, int64_t n_kv,
+                    int64_t block_m, int64_t block_n, int64_t tile_m, int64_t tile_n,
+                    int32_t* row_ptr, int32_t* col_idx, int32_t* col_ptr,
+                    int32_t* row_idx, int32_t* nnz_out, void* stream);
+
+/* Tile sizes (tile_m, tile_n) whose plan the given pass expects.
+ * pass: 0 = forward, 1 = backward dQ (CSR), 2 = backward dK/dV (CSC),
+ * 3 = decode (n_q == 1). */
+int sbfa_plan_tiles(int pass, int dtype, int64_t head_dim, int64_t n_q,
+                    int64_t* tile_m, int64_t* tile_n);
+
+/* ---------------------------------------------------------------------------
+ * Attention
+ * ------------------------------------------------------------------------- */
+
+/* Common shape/semantic arguments, in this order, for the calls below:
+ *   B, H, n_q, n_kv, head_dim, dtype, softmax_scale, is_causal, sink, window,
+ *   block_mask, block_m, block_n
+ */
+
+/* Forward: O = softmax(Q K^T * scale  masked) V, LSE = natural-log
+ * log-sum-exp per row (0 for empty rows).  Replaces _fwd_kernel and its
+ * launch in _BlockSparseFlashAttention.forward
+ * (sparse_triton_kernel.py:231-352, 652-682).
+ * row_ptr/col_idx: plan of pass 0 for this mask. */
+int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+             int64_t B, int64_t H, int64_t n_q, int64_t n_kv, int64_t head_dim,
+             int dtype, float softmax_scale, int is_causal, int64_t sink,
+             int64_t window, const int32_t* block_mask, int64_t block_m,
+             int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
+             void* stream);
+
+/* Backward: dQ, dK, dV (written, not accumulated) from Q, K, V, O, dO and
+ * the forward's LSE.  Replaces _bwd_preprocess_kernel, _bwd_dkdv_kernel,
+ * _bwd_dq_kernel and their launches (sparse_triton_kernel.py:355-601,
+ * 694-779).  delta_ws: caller scratch, fp32[B*H*n_q].
+ * dq_row_ptr/dq_col_idx: plan of pass 1; kv_col_ptr/kv_row_idx: plan of
+ * pass 2 (may be the same plan when the tiles agree). */
+int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
+             const float* lse, const void* dout, void* dq, void* dk, void* dv,
+             float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
+             int64_t head_dim, int dtype, float softmax_scale, int is_causal,
+             int64_t sink, int64_t window, const int32_t* block_mask,
+             int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
+             const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
+             const int32_t* kv_row_idx, void* stream);
+
+/* Split-KV decode for n_q == 1 (the upstream path is _fwd_kernel with
+ * N_Q = 1, BLOCK_M = 1: benchmark.py:799-804 -> sparse_triton_kernel.py:231).
+ * Reads only the K/V rows the query can see.  row_ptr/col_idx: plan of
+ * pass 3.  split_ws: caller scratch of sbfa_decode_workspace_bytes() bytes.
+ * lse may be NULL. */
+int sbfa_decode(const void* q, const void* k, const void* v, void* o, float* lse,
+                int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
+                float softmax_scale, int is_causal, int64_t sink, int64_t window,
+                const int32_t* block_mask, int64_t block_m, int64_t block_n,
+                const int32_t* row_ptr, const int32_t* col_idx, void* split_ws,
+                int64_t split_ws_bytes, void* stream);
+
+/* Scratch bytes sbfa_decode needs for this shape. */
+int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
+                                    int64_t head_dim, int64_t block_n);
+
+/* 1 if sbfa_decode has a kernel for (dtype, head_dim), else 0 (callers then
+ * run sbfa_fwd with n_q == 1, as upstream does). */
+int sbfa_decode_supported(int dtype, int64_t head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SBFA_H_ */
