@@ -59,7 +59,7 @@ __device__ __forceinline__ void load_rows(A* dst, int ld, const T* src, int r0, 
 template <typename T, int DPL>
 __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    T* __restrict__ o, float* __restrict__ lse, int D, float scale_f, MaskParams mp,
+    T* __restrict__ o, float* __restrict__ lse, int D, double scale_f, MaskParams mp,
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -175,7 +175,7 @@ template <typename T, int DPL>
 __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const T* __restrict__ dout, const float* __restrict__ lse,
-    const float* __restrict__ delta, T* __restrict__ dq, int D, float scale_f, MaskParams mp,
+    const float* __restrict__ delta, T* __restrict__ dq, int D, double scale_f, MaskParams mp,
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const T* __restrict__ dout, const float* __restrict__ lse,
     const float* __restrict__ delta, T* __restrict__ dk, T* __restrict__ dv, int D,
-    float scale_f, MaskParams mp, const int32_t* __restrict__ col_ptr,
+    double scale_f, MaskParams mp, const int32_t* __restrict__ col_ptr,
     const int32_t* __restrict__ row_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -392,7 +392,7 @@ int set_smem(K kernel, size_t bytes) {
 
 template <typename T, int DPL>
 int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH,
-               int D, float scale, const MaskParams& mp, const int32_t* row_ptr,
+               int D, double scale, const MaskParams& mp, const int32_t* row_ptr,
                const int32_t* col_idx, cudaStream_t s) {
   auto kern = fwd_generic_kernel<T, DPL>;
   size_t sm = fwd_smem<T>(D);
@@ -409,7 +409,7 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
 template <typename T, int DPL>
 int launch_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
                const void* dout, void* dq, void* dk, void* dv, float* delta, int BH, int D,
-               float scale, const MaskParams& mp, const int32_t* dq_row_ptr,
+               double scale, const MaskParams& mp, const int32_t* dq_row_ptr,
                const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
                const int32_t* kv_row_idx, cudaStream_t s) {
   const int64_t rows = (int64_t)BH * mp.n_q;
@@ -448,7 +448,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
 
 template <typename T>
 int dispatch_fwd(int D, const void* q, const void* k, const void* v, void* o, float* lse,
-                 int BH, float scale, const MaskParams& mp, const int32_t* rp,
+                 int BH, double scale, const MaskParams& mp, const int32_t* rp,
                  const int32_t* ci, cudaStream_t s) {
   if (D <= 32) return launch_fwd<T, 1>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
   if (D <= 64) return launch_fwd<T, 2>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
@@ -459,7 +459,7 @@ int dispatch_fwd(int D, const void* q, const void* k, const void* v, void* o, fl
 template <typename T>
 int dispatch_bwd(int D, const void* q, const void* k, const void* v, const void* o,
                  const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                 int BH, float scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
+                 int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
                  const int32_t* c, const int32_t* d, cudaStream_t s) {
   if (D <= 32)
     return launch_bwd<T, 1>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
@@ -486,7 +486,7 @@ bool generic_supports(int dtype, int64_t D) {
 }
 
 int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o,
-                float* lse, int BH, float scale, const MaskParams& mp, const int32_t* rp,
+                float* lse, int BH, double scale, const MaskParams& mp, const int32_t* rp,
                 const int32_t* ci, cudaStream_t s) {
   switch (dtype) {
     case SBFA_F16: return dispatch_fwd<__half>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
@@ -499,7 +499,7 @@ int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, v
 
 int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                int BH, float scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
+                int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
                 const int32_t* c, const int32_t* d, cudaStream_t s) {
   switch (dtype) {
     case SBFA_F16:

@@ -18,11 +18,11 @@ namespace sbfa {
 int generic_tiles(int pass, int64_t* tm, int64_t* tn);
 bool generic_supports(int dtype, int64_t D);
 int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o,
-                float* lse, int BH, float scale, const MaskParams& mp, const int32_t* rp,
+                float* lse, int BH, double scale, const MaskParams& mp, const int32_t* rp,
                 const int32_t* ci, cudaStream_t s);
 int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                int BH, float scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
+                int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
                 const int32_t* c, const int32_t* d, cudaStream_t s);
 // decode.cu
 int decode_tile();
@@ -255,7 +255,7 @@ extern "C" int sbfa_plan_tiles(int pass, int dtype, int64_t head_dim, int64_t n_
 
 extern "C" int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
                         int64_t B, int64_t H, int64_t n_q, int64_t n_kv, int64_t head_dim,
-                        int dtype, float softmax_scale, int is_causal, int64_t sink,
+                        int dtype, double softmax_scale, int is_causal, int64_t sink,
                         int64_t window, const int32_t* block_mask, int64_t block_m,
                         int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
                         void* stream) {
@@ -279,7 +279,7 @@ extern "C" int sbfa_fwd(const void* q, const void* k, const void* v, void* o, fl
 extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
                         const float* lse, const void* dout, void* dq, void* dk, void* dv,
                         float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
-                        int64_t head_dim, int dtype, float softmax_scale, int is_causal,
+                        int64_t head_dim, int dtype, double softmax_scale, int is_causal,
                         int64_t sink, int64_t window, const int32_t* block_mask,
                         int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
                         const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
@@ -324,7 +324,7 @@ extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_k
 
 extern "C" int sbfa_decode(const void* q, const void* k, const void* v, void* o, float* lse,
                            int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
-                           float softmax_scale, int is_causal, int64_t sink, int64_t window,
+                           double softmax_scale, int is_causal, int64_t sink, int64_t window,
                            const int32_t* block_mask, int64_t block_m, int64_t block_n,
                            const int32_t* row_ptr, const int32_t* col_idx, void* split_ws,
                            int64_t split_ws_bytes, void* stream) {

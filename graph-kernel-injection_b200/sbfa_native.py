@@ -26,7 +26,7 @@ _DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32, tor
 _lib: Optional[ctypes.CDLL] = None
 _lock = threading.Lock()
 
-_i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+_i64, _i32, _f64, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_double, ctypes.c_void_p
 
 _SIGNATURES = {
     "sbfa_abi_version": ([], _i32),
@@ -42,12 +42,12 @@ _SIGNATURES = {
                         _i32),
     "sbfa_plan_tiles": ([_i32, _i32, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
                         _i32),
-    "sbfa_fwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i32,
+    "sbfa_fwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _f64, _i32,
                   _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp], _i32),
     "sbfa_bwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
-                  _i64, _i32, _f32, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
+                  _i64, _i32, _f64, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
                   _vp], _i32),
-    "sbfa_decode": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _i64,
+    "sbfa_decode": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f64, _i32, _i64,
                      _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _i32),
     "sbfa_decode_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "sbfa_decode_supported": ([_i32, _i64], _i32),

@@ -128,7 +128,7 @@ int sbfa_plan_tiles(int pass, int dtype, int64_t head_dim, int64_t n_q,
  * row_ptr/col_idx: plan of pass 0 for this mask. */
 int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
              int64_t B, int64_t H, int64_t n_q, int64_t n_kv, int64_t head_dim,
-             int dtype, float softmax_scale, int is_causal, int64_t sink,
+             int dtype, double softmax_scale, int is_causal, int64_t sink,
              int64_t window, const int32_t* block_mask, int64_t block_m,
              int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
              void* stream);
@@ -142,7 +142,7 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
 int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              const float* lse, const void* dout, void* dq, void* dk, void* dv,
              float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
-             int64_t head_dim, int dtype, float softmax_scale, int is_causal,
+             int64_t head_dim, int dtype, double softmax_scale, int is_causal,
              int64_t sink, int64_t window, const int32_t* block_mask,
              int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
              const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
@@ -155,7 +155,7 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
  * lse may be NULL. */
 int sbfa_decode(const void* q, const void* k, const void* v, void* o, float* lse,
                 int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
-                float softmax_scale, int is_causal, int64_t sink, int64_t window,
+                double softmax_scale, int is_causal, int64_t sink, int64_t window,
                 const int32_t* block_mask, int64_t block_m, int64_t block_n,
                 const int32_t* row_ptr, const int32_t* col_idx, void* split_ws,
                 int64_t split_ws_bytes, void* stream);

@@ -2,7 +2,8 @@
 
 Tolerances (written per dtype, from the upstream verification protocol
 and the north-star bar):
-  * float64: 1e-9 absolute (exact arithmetic path);
+  * float64: forward 1e-9; gradients 1e-6 (the backward reads the fp32 LSE
+    and Delta the upstream format stores, sparse_triton_kernel.py:653,716);
   * float32: forward atol = rtol = 1e-4 (benchmark.py:166-195), gradients
     atol = rtol = 1e-3 (benchmark.py:322-355);
   * float16 / bfloat16: max-abs <= 2e-2 * max(1, max|ref|) and
@@ -33,7 +34,8 @@ def close(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, kind: str = 
     ref = ref.double().cpu()
     assert torch.isfinite(got).all(), "non-finite output"
     if dtype == torch.float64:
-        assert torch.allclose(got, ref, atol=1e-9, rtol=1e-9), (got - ref).abs().max()
+        tol = 1e-9 if kind == "fwd" else 1e-6
+        assert torch.allclose(got, ref, atol=tol, rtol=tol), (got - ref).abs().max()
     elif dtype == torch.float32:
         tol = 1e-4 if kind == "fwd" else 1e-3
         assert torch.allclose(got, ref, atol=tol, rtol=tol), (got - ref).abs().max()
@@ -259,3 +261,26 @@ def test_errors_are_raised():
     with pytest.raises(ValueError, match="unsupported dtype"):
         stk.block_sparse_attention(q.int(), k.int(), v.int(), torch.ones(
             4, 4, dtype=torch.int32, device=DEV), block_m=16, block_n=16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+def test_tensor_core_path_empty_rows(dtype, D):
+    """bf16/fp16 with D in {64, 128} runs the tcgen05 forward: a query tile
+    with no kept block, rows with no visible key inside kept tiles, and a
+    ragged last tile must all match the oracle (zeros where nothing is
+    visible)."""
+    n_q, n_kv, bm = 384, 300, 128
+    q, k, v, do = _inputs(2, 2, n_q, n_kv, D, dtype, seed=9)
+    mask = torch.ones(3, 3, dtype=torch.int32, device=DEV)
+    mask[0, :] = 0          # first query tile sees nothing
+    mask[2, 0] = 0
+    for causal in (False, True):
+        o, dq, dk, dv = run(q, k, v, mask, bm, bm, causal, 0, 40, do=do)
+        ro, rdq, rdk, rdv = orc.attention_forward_backward(
+            q.double().cpu(), k.double().cpu(), v.double().cpu(), do.double().cpu(), mask.cpu(),
+            block_m=bm, block_n=bm, is_causal=causal, sink_size=0, window_size=40)
+        assert torch.equal(o[:, :, :bm].float(), torch.zeros_like(o[:, :, :bm].float()))
+        for a, b, kind in ((o, ro, "fwd"), (dq, rdq, "bwd"), (dk, rdk, "bwd"), (dv, rdv, "bwd")):
+            close(a, b, dtype, kind)
+    assert native.device_status() == 0
