@@ -316,13 +316,14 @@ def bench_fwdbwd(dist, args, pk, src):
             h.copy_(d, non_blocking=True)
 
     e_steps = max(2, min(args.steps, 5))
-    e_ms, _, _ = time_steps(dist, e2e_step, e_steps, 1)
+    e_ms = float("nan") if args.no_e2e else time_steps(dist, e2e_step, e_steps, 1)[0]
     del dq_, dk_, dv_
     bytes_h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
     bytes_d2h = sum(t.numel() * t.element_size() for t in out_h)
-    e2e = {"value": round(3.5 * F * dist.world * e_steps / (e_ms / 1e3) / 1e12, 3),
-           "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d, "d2h_bytes_per_step": bytes_d2h,
-           "ms_per_step": round(e_ms / e_steps, 3)}
+    e2e = None if args.no_e2e else {
+        "value": round(3.5 * F * dist.world * e_steps / (e_ms / 1e3) / 1e12, 3),
+        "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d, "d2h_bytes_per_step": bytes_d2h,
+        "ms_per_step": round(e_ms / e_steps, 3)}
     rl = roofline(per_kernel, F, pk, src, sustained=True)
     res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
                nnz=nnz, flops_fwd=F, finite=finite, per_kernel=per_kernel)
@@ -427,7 +428,7 @@ def base_line(args, world):
             "data": "synthetic (seeded N(0,1) q/k/v/dO, BASELINE config 2 shapes)",
             "config": {"workload": "cfg2 sparse prefill fwd+bwd: B=4 H=32 N=16384 D=128 bf16 "
                                    "S=4 W=2048 BM=BN=128 per rank",
-                       "global_batch": 4 * world, "seq_len": 16384, "heads": 32,
+                       "global_batch": 4 * world, "seq_len": 16384, "heads": CFG2["H"],
                        "head_dim": 128, "parallelism": f"(batch,head) shards x{world}",
                        "l2": "inputs exceed L2 (537 MB per tensor); no flush"}}
 
@@ -459,7 +460,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["all", "fwdbwd", "fwd", "decode"], default="all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="override the per-rank head count (small cases for profiling)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
+    if args.heads > 0:
+        for cfg in (CFG2, CFG3, CFG4):
+            cfg["H"] = args.heads
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -1,19 +1,30 @@
 // Tensor-core block-sparse attention for sm_100a: TMA + tcgen05 + TMEM.
 //
 // Forward (replaces upstream _fwd_kernel, sparse_triton_kernel.py:231-352).
-// One CTA per (128-row query tile, batch*head), 192 threads:
-//   warp 0      TMA producer: Q once, then K and V tiles of the kept key
-//               tiles (plan CSR row) into STAGES-deep rings;
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
-//               S buffers, O += P_j V_j into the TMEM O accumulator;
-//   warps 2-5   softmax: thread t owns query row t (the TMEM lane it may
-//               read), loads its 128 scores with tcgen05.ld, applies the
-//               token rule on boundary tiles only, runs the online softmax
-//               in base 2, rescales its O row in TMEM only when the running
-//               max grew by more than 2^8, writes P (bf16/fp16) to shared
-//               memory in the 128-byte-swizzled K-major layout the MMA reads.
-// Pipelining: QK_{j+2} is issued as soon as softmax released S buffer j%2,
-// so the tensor core computes the next scores while softmax runs.
+// One CTA per (pair of 128-row query tiles A/B, batch*head), 384 threads in
+// three warpgroups (registers rebalanced with setmaxnreg: 64 / 208 / 208):
+//   warp 0      TMA producer: Q_A, Q_B once, then K_j, V_j of every kept key
+//               tile (plan CSR row, 256x128 tiles) into one STAGES-deep ring
+//               that alternates K and V tiles;
+//   warp 1      MMA issuer (one thread): S_X = Q_X K_j^T into TMEM, and
+//               O_X += P_X V_j with P_X read straight from TMEM;
+//   warps 2-3   idle;
+//   warps 4-7   softmax for tile A, warps 8-11 for tile B: thread t of a group
+//               owns query row t (its TMEM lane), loads the row's 128 scores
+//               with tcgen05.ld, masks them with a 128-bit visibility mask
+//               built from intervals (token rule, sequence end) and the lifted
+//               block mask on partial tiles, runs the online softmax in base 2,
+//               rescales its O row in TMEM only when the running max grew by
+//               more than 2^8, and writes P (bf16/fp16) into the upper half of
+//               its S columns with tcgen05.st.
+// Schedule of the MMA thread per key tile j:
+//   PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j)
+// so softmax A(j) overlaps PV_B(j-1) + QK_B(j) and vice versa.  MMAs from one
+// thread execute in issue order, so QK_X(j) overwrites S_X/P_X only after
+// PV_X(j-1) has read P_X, and when S_X(j) is complete O_X already holds
+// PV_X(j-1) (no extra barrier for the O rescale).
+// Epilogue: O rows are normalised, staged in the Q buffer (128-byte swizzle)
+// and written with a TMA store; LSE rows are stored directly.
 // Numerics as upstream: natural-log LSE = m + log(l), empty rows give
 // O = 0 and LSE = 0, P is rounded to the input type before P V.
 #include <cuda.h>
@@ -29,43 +40,39 @@ namespace {
 
 using namespace tc;
 
-constexpr int kTM = 128;  // query rows per tile
-constexpr int kTN = 128;  // keys per tile
-constexpr int kFwdThreads = 192;
+constexpr int kTM = 128;   // rows per query tile (one TMEM lane per row)
+constexpr int kPair = 2;   // query tiles per CTA
+constexpr int kTN = 128;   // keys per key tile
+constexpr int kFwdThreads = 384;
+constexpr int kRegsCtl = 64;       // producer / MMA warpgroup
+constexpr int kRegsSoftmax = 208;  // each softmax warpgroup (128*64 + 256*208 <= 384*168)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr uint32_t kTmemCols = 512;  // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 
 template <int D, int STAGES>
 struct FwdLayout {
-  static constexpr uint32_t kTile = kTM * D * 2;  // one 128-row tile of Q, K or V
-  static constexpr uint32_t Q = 0;
-  static constexpr uint32_t K0 = Q + kTile;
-  static constexpr uint32_t V0 = K0 + STAGES * kTile;
-  static constexpr uint32_t P = V0 + STAGES * kTile;
-  static constexpr uint32_t BAR = P + kTM * kTN * 2;
-  // barrier slots
+  static constexpr uint32_t kTile = kTM * D * 2;       // 128 rows x D, 16-bit
+  static constexpr uint32_t Q = 0;                     // Q_A, Q_B; O staging in the epilogue
+  static constexpr uint32_t KV = Q + kPair * kTile;    // ring: K_0, V_0, K_1, V_1, ...
+  static constexpr uint32_t BAR = KV + STAGES * kTile;
   static constexpr int kQFull = 0;
-  static constexpr int kKFull = 1;
-  static constexpr int kKEmpty = 1 + STAGES;
-  static constexpr int kVFull = 1 + 2 * STAGES;
-  static constexpr int kVEmpty = 1 + 3 * STAGES;
-  static constexpr int kSFull = 1 + 4 * STAGES;   // 2
-  static constexpr int kSEmpty = 3 + 4 * STAGES;  // 2
-  static constexpr int kPFull = 5 + 4 * STAGES;
-  static constexpr int kPVDone = 6 + 4 * STAGES;
-  static constexpr int kDrain = 7 + 4 * STAGES;
-  static constexpr int kNumBars = 8 + 4 * STAGES;
+  static constexpr int kKVFull = 1;
+  static constexpr int kKVEmpty = 1 + STAGES;
+  static constexpr int kSFull = 1 + 2 * STAGES;  // [2]
+  static constexpr int kPFull = 3 + 2 * STAGES;  // [2]
+  static constexpr int kOFull = 5 + 2 * STAGES;  // [2]
+  static constexpr int kDrain = 7 + 2 * STAGES;
+  static constexpr int kNumBars = 8 + 2 * STAGES;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;  // [0] TMEM base, [1] abort flag
   static constexpr uint32_t kBytes = MISC + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;     // room to align the base to 1 KB
 };
 
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+D)
-
 __device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, int* status) {
-  // used only to drain our own in-flight async work before exit: ignores the
-  // abort flag but is still bounded
+  // drains our own in-flight async work before exit: ignores the abort flag
+  // but is still bounded
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
@@ -77,11 +84,44 @@ __device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, in
   return true;
 }
 
+// Visibility of the 128 keys [k0, k0+128) for one query row, bit c of
+// vis[c/32] = key k0 + c: sequence end, token rule when causal (at most two
+// intervals: sink and window), lifted block mask on partial tiles.
+__device__ __forceinline__ void row_visibility(uint32_t vis[4], const MaskParams& mp, int row,
+                                               int k0, bool partial) {
+  if (row >= mp.n_q) {
+    vis[0] = vis[1] = vis[2] = vis[3] = 0u;
+    return;
+  }
+  const int end = min(mp.n_kv - k0, kTN);
+  int lo1 = 0, hi1 = end, lo2 = 0, hi2 = 0;
+  if (mp.causal) {
+    const int qpos = mp.q_off + row;
+    const int cend = min(end, qpos - k0 + 1);
+    hi1 = min(cend, mp.sink - k0);
+    lo2 = max(qpos - mp.window + 1 - k0, 0);
+    hi2 = cend;
+  }
+#pragma unroll
+  for (int w = 0; w < 4; ++w) vis[w] = range_bits(lo1, hi1, 32 * w) | range_bits(lo2, hi2, 32 * w);
+  if (partial) {
+    const int32_t* mrow = mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb;
+    const int b0 = k0 / mp.block_n;
+    const int b1 = min((k0 + kTN - 1) / mp.block_n, mp.n_kb - 1);
+    for (int b = b0; b <= b1; ++b) {
+      if (__ldg(mrow + b) != 0) continue;
+      const int lo = b * mp.block_n - k0, hi = lo + mp.block_n;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) vis[w] &= ~range_bits(lo, hi, 32 * w);
+    }
+  }
+}
+
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmv, T* __restrict__ o,
-                  float* __restrict__ lse, float scale_log2, MaskParams mp,
+                  const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
+                  T* __restrict__ o, float* __restrict__ lse, float scale_log2, MaskParams mp,
                   const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
                   int* status) {
   using L = FwdLayout<D, STAGES>;
@@ -99,20 +139,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ti = blockIdx.x;
+  const int pair = blockIdx.x;
   const int bh = blockIdx.y;
-  const int e0 = row_ptr[ti];
-  const int n = row_ptr[ti + 1] - e0;
+  const int row0 = pair * kPair * kTM;
+  const int e0 = row_ptr[pair];
+  const int n = row_ptr[pair + 1] - e0;
 
-  if (n == 0) {  // no kept key tile: O = 0, LSE = 0 for every row of the tile
-    for (int idx = threadIdx.x; idx < kTM * (D / 8); idx += blockDim.x) {
+  if (n == 0) {  // no kept key tile: O = 0, LSE = 0 for every row of the pair
+    for (int idx = threadIdx.x; idx < kPair * kTM * (D / 8); idx += blockDim.x) {
       const int rr = idx / (D / 8), cc = idx % (D / 8);
-      const int row = ti * kTM + rr;
+      const int row = row0 + rr;
       if (row < mp.n_q)
         reinterpret_cast<uint4*>(o + ((size_t)bh * mp.n_q + row) * D)[cc] = make_uint4(0, 0, 0, 0);
     }
-    for (int rr = threadIdx.x; rr < kTM; rr += blockDim.x) {
-      const int row = ti * kTM + rr;
+    for (int rr = threadIdx.x; rr < kPair * kTM; rr += blockDim.x) {
+      const int row = row0 + rr;
       if (row < mp.n_q) lse[(size_t)bh * mp.n_q + row] = 0.f;
     }
     return;
@@ -121,17 +162,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(bar(L::kQFull), 1);
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar(L::kKFull + s), 1);
-      mbar_init(bar(L::kKEmpty + s), 1);
-      mbar_init(bar(L::kVFull + s), 1);
-      mbar_init(bar(L::kVEmpty + s), 1);
+      mbar_init(bar(L::kKVFull + s), 1);
+      mbar_init(bar(L::kKVEmpty + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(L::kSFull + b), 1);
-      mbar_init(bar(L::kSEmpty + b), 128);
+    for (int x = 0; x < kPair; ++x) {
+      mbar_init(bar(L::kSFull + x), 1);
+      mbar_init(bar(L::kPFull + x), 128);
+      mbar_init(bar(L::kOFull + x), 1);
     }
-    mbar_init(bar(L::kPFull), 128);
-    mbar_init(bar(L::kPVDone), 1);
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
     mbar_init_fence();
@@ -145,149 +183,169 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp < 4) {
+   regs_dec<kRegsCtl>();
+   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      mbar_expect_tx(bar(L::kQFull), L::kTile);
-      for (int r = 0; r < kBoxes; ++r)
-        tma_load_3d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kTM, bh);
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+      mbar_expect_tx(bar(L::kQFull), kPair * L::kTile);
+      for (int x = 0; x < kPair; ++x)
+        for (int r = 0; r < kBoxes; ++r)
+          tma_load_3d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
+                      row0 + x * kTM, bh);
+      int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
+      bool ok = true;
+      for (int j = 0; ok && j < n; ++j) {
         const int kt = plan_index(col_idx[e0 + j]);
-        if (j >= STAGES && !wait_bar(bar(L::kKEmpty + s), ph ^ 1u, abort_flag, status)) break;
-        mbar_expect_tx(bar(L::kKFull + s), L::kTile);
-        for (int r = 0; r < kBoxes; ++r)
-          tma_load_3d(sb + L::K0 + s * L::kTile + r * 16384u, &tmk, bar(L::kKFull + s), 64 * r,
-                      kt * kTN, bh);
-        k_issued = j + 1;
-        if (j >= STAGES && !wait_bar(bar(L::kVEmpty + s), ph ^ 1u, abort_flag, status)) break;
-        mbar_expect_tx(bar(L::kVFull + s), L::kTile);
-        for (int r = 0; r < kBoxes; ++r)
-          tma_load_3d(sb + L::V0 + s * L::kTile + r * 16384u, &tmv, bar(L::kVFull + s), 64 * r,
-                      kt * kTN, bh);
-        v_issued = j + 1;
+        for (int part = 0; part < 2; ++part) {
+          const int e = 2 * j + part;
+          const int s = e % STAGES, f = e / STAGES;
+          if (f > 0 && !wait_bar(bar(L::kKVEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(bar(L::kKVFull + s), L::kTile);
+          for (int r = 0; r < kBoxes; ++r)
+            tma_load_3d(sb + L::KV + s * L::kTile + r * 16384u, part == 0 ? &tmk : &tmv,
+                        bar(L::kKVFull + s), 64 * r, kt * kTN, bh);
+          issued = e + 1;
+        }
       }
       // wait for our own copies still in flight (all consumed on success)
       wait_bar_drain(bar(L::kQFull), 0, status);
       for (int s = 0; s < STAGES; ++s) {
-        const int fk = k_issued > s ? (k_issued - 1 - s) / STAGES + 1 : 0;
-        const int fv = v_issued > s ? (v_issued - 1 - s) / STAGES + 1 : 0;
-        if (fk) wait_bar_drain(bar(L::kKFull + s), (uint32_t)((fk - 1) & 1), status);
-        if (fv) wait_bar_drain(bar(L::kVFull + s), (uint32_t)((fv - 1) & 1), status);
+        const int fills = issued > s ? (issued - 1 - s) / STAGES + 1 : 0;
+        if (fills) wait_bar_drain(bar(L::kKVFull + s), (uint32_t)((fills - 1) & 1), status);
       }
-    }
-  } else if (warp == 1) {
+   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status);
-      auto issue_qk = [&](int t) -> bool {
-        const int s = t % STAGES, b = t & 1;
-        if (!wait_bar(bar(L::kKFull + s), (uint32_t)((t / STAGES) & 1), abort_flag, status))
-          return false;
-        if (t >= 2 &&
-            !wait_bar(bar(L::kSEmpty + b), (uint32_t)(((t - 2) >> 1) & 1), abort_flag, status))
-          return false;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)b * 128u;
+    {
+      auto kv_wait = [&](int e) -> bool {
+        return wait_bar(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
+                        status);
+      };
+      auto qk = [&](int x, int e) {
+        const uint32_t kbase = sb + L::KV + (uint32_t)(e % STAGES) * L::kTile;
+        const uint32_t qbase = sb + L::Q + (uint32_t)x * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(d_tmem, desc_kmajor(sb + L::Q + off),
-                     desc_kmajor(sb + L::K0 + s * L::kTile + off), kIdescQK, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + 128u * x, desc_kmajor(qbase + off), desc_kmajor(kbase + off), kIdescQK,
+                     kk > 0 ? 1u : 0u);
         }
-        tc_commit(bar(L::kSFull + b));
-        tc_commit(bar(L::kKEmpty + s));
-        return true;
       };
-      if (ok) ok = issue_qk(0);
-      if (ok && n > 1) ok = issue_qk(1);
-      for (int j = 0; ok && j < n; ++j) {
-        const int s = j % STAGES;
-        if (!wait_bar(bar(L::kPFull), (uint32_t)(j & 1), abort_flag, status)) break;
-        if (!wait_bar(bar(L::kVFull + s), (uint32_t)((j / STAGES) & 1), abort_flag, status)) break;
-        tc_fence_after();
+      auto pv = [&](int x, int e, bool acc) {
+        const uint32_t vbase = sb + L::KV + (uint32_t)(e % STAGES) * L::kTile;
 #pragma unroll
-        for (int kk = 0; kk < kTN / 16; ++kk) {
-          const uint32_t poff = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + 256u, desc_kmajor(sb + L::P + poff),
-                     desc_mnmajor(sb + L::V0 + s * L::kTile + (uint32_t)kk * 2048u, 16384u),
-                     kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kTN / 16; ++kk)
+          mma_f16_ts(tmem + 256u + 128u * x, tmem + 128u * x + 64u + 8u * kk,
+                     desc_mnmajor(vbase + (uint32_t)kk * 2048u, 16384u), kIdescPV,
+                     (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status) && kv_wait(0);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        tc_commit(bar(L::kSFull + 0));
+        qk(1, 0);
+        tc_commit(bar(L::kSFull + 1));
+        tc_commit(bar(L::kKVEmpty + 0));
+      }
+      for (int j = 1; ok && j < n; ++j) {
+        const int ev = 2 * j - 1, ek = 2 * j;
+        const uint32_t ph = (uint32_t)((j - 1) & 1);
+        if (!(kv_wait(ev) && kv_wait(ek))) { ok = false; break; }
+        if (!wait_bar(bar(L::kPFull + 0), ph, abort_flag, status)) { ok = false; break; }
+        tc_fence_after();
+        pv(0, ev, j > 1);
+        qk(0, ek);
+        tc_commit(bar(L::kSFull + 0));
+        if (!wait_bar(bar(L::kPFull + 1), ph, abort_flag, status)) { ok = false; break; }
+        tc_fence_after();
+        pv(1, ev, j > 1);
+        tc_commit(bar(L::kKVEmpty + ev % STAGES));
+        qk(1, ek);
+        tc_commit(bar(L::kSFull + 1));
+        tc_commit(bar(L::kKVEmpty + ek % STAGES));
+      }
+      if (ok) {
+        const int ev = 2 * n - 1;
+        const uint32_t ph = (uint32_t)((n - 1) & 1);
+        ok = kv_wait(ev) && wait_bar(bar(L::kPFull + 0), ph, abort_flag, status);
+        if (ok) {
+          tc_fence_after();
+          pv(0, ev, n > 1);
+          tc_commit(bar(L::kOFull + 0));
+          ok = wait_bar(bar(L::kPFull + 1), ph, abort_flag, status);
         }
-        tc_commit(bar(L::kPVDone));
-        tc_commit(bar(L::kVEmpty + s));
-        if (j + 2 < n) ok = issue_qk(j + 2);
+        if (ok) {
+          tc_fence_after();
+          pv(1, ev, n > 1);
+          tc_commit(bar(L::kOFull + 1));
+          tc_commit(bar(L::kKVEmpty + ev % STAGES));
+        }
       }
       tc_commit(bar(L::kDrain));
       wait_bar_drain(bar(L::kDrain), 0, status);
     }
+   }
   } else {
-    // ------------------------------------------------------------ softmax
+    regs_inc<kRegsSoftmax>();
+    // ------------------------------------------------------------ softmax A / B
+    const int x = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int row = ti * kTM + r;
-    const int qpos = mp.q_off + row;
+    const int row = row0 + x * kTM + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + 128u * x;
+    const uint32_t t_p = t_s + 64u;
+    const uint32_t t_o = tmem + lane_base + 256u + 128u * x;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       const int32_t ent = col_idx[e0 + j];
-      const int kt = plan_index(ent);
+      const int k0 = plan_index(ent) * kTN;
       const bool partial = plan_partial(ent);
-      const int b = j & 1;
+      uint32_t vis[4];
+      row_visibility(vis, mp, row, k0, partial);
       ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kSFull + b), (uint32_t)((j >> 1) & 1), abort_flag, status));
+                      wait_bar(bar(L::kSFull + x), (uint32_t)(j & 1), abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      float x[kTN];
-      {
-        uint32_t xr[kTN];
+      uint32_t sv[kTN];
 #pragma unroll
-        for (int c = 0; c < kTN / 32; ++c)
-          tmem_ld32(tmem + lane_base + (uint32_t)b * 128u + 32u * c, xr + 32 * c);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < kTN; ++c) x[c] = __uint_as_float(xr[c]);
-      }
-      tc_fence_before();
-      mbar_arrive(bar(L::kSEmpty + b));
-
-      const int k0 = kt * kTN;
-      const bool full = row < mp.n_q && k0 + kTN - 1 < mp.n_kv && !partial &&
-                        (!mp.causal || (k0 + kTN - 1 <= qpos &&
-                                        (k0 + kTN - 1 < mp.sink || k0 >= qpos - mp.window + 1)));
-      if (!full) {
-#pragma unroll
-        for (int c = 0; c < kTN; ++c)
-          if (!visible(mp, row, k0 + c, partial)) x[c] = -INFINITY;
-      }
+      for (int c = 0; c < kTN / 32; ++c) tmem_ld32(t_s + 32u * c, sv + 32 * c);
+      tmem_wait_ld();
       float rmax = -INFINITY;
+      if ((vis[0] & vis[1] & vis[2] & vis[3]) == 0xffffffffu) {
 #pragma unroll
-      for (int c = 0; c < kTN; ++c) {
-        x[c] *= scale_log2;
-        rmax = fmaxf(rmax, x[c]);
+        for (int c = 0; c < kTN; ++c) {
+          const float v = __uint_as_float(sv[c]) * scale_log2;
+          sv[c] = __float_as_uint(v);
+          rmax = fmaxf(rmax, v);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kTN; ++c) {
+          const float v = ((vis[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(sv[c]) * scale_log2
+                                                           : -INFINITY;
+          sv[c] = __float_as_uint(v);
+          rmax = fmaxf(rmax, v);
+        }
       }
       const float m_new = fmaxf(m_run, rmax);
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
-      bool pv_waited = false;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        ok = __all_sync(0xffffffffu, wait_bar(bar(L::kPVDone), (uint32_t)((j - 1) & 1),
-                                              abort_flag, status));
-        if (!ok) break;
-        pv_waited = true;
-        tc_fence_after();
+      if (__any_sync(0xffffffffu, need)) {
+        // O_X already holds PV_X(j-1): it completed before S_X(j) did
         const float alpha = need ? ex2(m_run - m_new) : 1.f;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t t[32];
-          tmem_ld32(tmem + lane_base + 256u + 32u * c, t);
+          tmem_ld32(t_o + 32u * c, t);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-          tmem_st32(tmem + lane_base + 256u + 32u * c, t);
+          tmem_st32(t_o + 32u * c, t);
         }
-        tmem_wait_st();
       }
       if (need) {
         l_run *= ex2(m_run - m_new);
@@ -295,59 +353,58 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       if (m_run == -INFINITY) m_run = m_new;  // first visible key: O row and l are still 0
       const bool dead = (m_run == -INFINITY);
-      uint32_t pk[kTN / 2];
       float rsum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kTN / 2; ++c) {
-        const float p0 = dead ? 0.f : ex2(x[2 * c] - m_run);
-        const float p1 = dead ? 0.f : ex2(x[2 * c + 1] - m_run);
-        rsum += p0 + p1;
-        pk[c] = pack2<T>(p0, p1);
-      }
-      l_run += rsum;
-      if (j > 0 && !pv_waited) {  // the single P buffer is free once P_{j-1} V_{j-1} is done
-        ok = __all_sync(0xffffffffu, wait_bar(bar(L::kPVDone), (uint32_t)((j - 1) & 1),
-                                              abort_flag, status));
-        if (!ok) break;
-      }
+      for (int c = 0; c < kTN / 32; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-      for (int ch = 0; ch < kTN / 8; ++ch) {
-        const uint32_t addr = sb + L::P + (uint32_t)(ch >> 3) * 16384u +
-                              sw128_offset((uint32_t)r, (uint32_t)(ch & 7) * 8u);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * ch]),
-                     "r"(pk[4 * ch + 1]), "r"(pk[4 * ch + 2]), "r"(pk[4 * ch + 3])
-                     : "memory");
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = dead ? 0.f : ex2(__uint_as_float(sv[32 * c + 2 * i]) - m_run);
+          const float p1 = dead ? 0.f : ex2(__uint_as_float(sv[32 * c + 2 * i + 1]) - m_run);
+          rsum += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        tmem_st16(t_p + 16u * c, pk);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      l_run += rsum;
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull));
+      mbar_arrive(bar(L::kPFull + x));
     }
-    if (ok)
-      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kPVDone), (uint32_t)((n - 1) & 1), abort_flag,
-                                            status));
+    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kOFull + x), 0, abort_flag, status));
     if (ok) {
       tc_fence_after();
       const bool valid = l_run > 0.f;
       const float inv = valid ? 1.f / l_run : 0.f;
-      T* orow = o + ((size_t)bh * mp.n_q + row) * D;
+      const uint32_t stage = sb + L::Q + (uint32_t)x * L::kTile;  // Q_X is no longer read
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t t[32];
-        tmem_ld32(tmem + lane_base + 256u + 32u * c, t);
+        tmem_ld32(t_o + 32u * c, t);
         tmem_wait_ld();
-        if (row < mp.n_q) {
-          uint32_t w[16];
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack2<T>(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack2<T>(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv);
+        const uint32_t region = stage + (uint32_t)((32 * c) >> 6) * 16384u;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t addr = region + sw128_offset((uint32_t)r, (uint32_t)((32 * c) & 63) + 8u * i);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * i]),
+                       "r"(w[4 * i + 1]), "r"(w[4 * i + 2]), "r"(w[4 * i + 3])
+                       : "memory");
         }
       }
       if (row < mp.n_q)
         lse[(size_t)bh * mp.n_q + row] = valid ? (m_run + log2f(l_run)) * kLn2 : 0.f;
+      fence_proxy_async_smem();
+      named_bar_sync(1 + x, 128);
+      if (r == 0) {
+        for (int b = 0; b < kBoxes; ++b)
+          tma_store_3d(&tmo, stage + (uint32_t)b * 16384u, 64 * b, row0 + x * kTM, bh);
+        bulk_commit();
+        bulk_wait_read0();
+      }
     }
   }
 
@@ -382,21 +439,22 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
                   float scale, const MaskParams& mp, const int32_t* rp, const int32_t* ci,
                   int* status, cudaStream_t s) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if (int rc = tc::make_tmap_3d(&mq, q, kBF16, D, (uint64_t)mp.n_q, (uint64_t)BH, kTM)) return rc;
   if (int rc = tc::make_tmap_3d(&mk, k, kBF16, D, (uint64_t)mp.n_kv, (uint64_t)BH, kTN)) return rc;
   if (int rc = tc::make_tmap_3d(&mv, v, kBF16, D, (uint64_t)mp.n_kv, (uint64_t)BH, kTN)) return rc;
+  if (int rc = tc::make_tmap_3d(&mo, o, kBF16, D, (uint64_t)mp.n_q, (uint64_t)BH, kTM)) return rc;
   using L = FwdLayout<D, STAGES>;
   auto kern = fwd_tc_kernel<T, D, STAGES>;
   if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)L::kAlloc),
                           "cudaFuncSetAttribute(fwd_tc)"))
     return rc;
-  dim3 grid(ceil_div_i(mp.n_q, kTM), BH);
+  dim3 grid(ceil_div_i(mp.n_q, kPair * kTM), BH);
   {
     LaunchScope ls("fwd_tc_kernel", s);
-    kern<<<grid, kFwdThreads, L::kAlloc, s>>>(mq, mk, mv, (T*)o, lse, scale * kLog2e, mp, rp, ci,
-                                             status);
+    kern<<<grid, kFwdThreads, L::kAlloc, s>>>(mq, mk, mv, mo, (T*)o, lse, scale * kLog2e, mp, rp,
+                                             ci, status);
   }
   return check_launch("fwd_tc_kernel");
 }
@@ -431,8 +489,7 @@ bool tc_supports(int pass, int dtype, int64_t D) {
 }
 
 int tc_tiles(int pass, int64_t* tm, int64_t* tn) {
-  (void)pass;
-  *tm = kTM;
+  *tm = pass == 0 ? kPair * kTM : kTM;
   *tn = kTN;
   return SBFA_OK;
 }
@@ -442,11 +499,11 @@ int tc_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* 
            int* status, cudaStream_t s) {
   const bool bf = dtype == SBFA_BF16;
   if (D == 128)
-    return bf ? launch_fwd_tc<__nv_bfloat16, 128, 2>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
-              : launch_fwd_tc<__half, 128, 2>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
+    return bf ? launch_fwd_tc<__nv_bfloat16, 128, 5>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
+              : launch_fwd_tc<__half, 128, 5>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
   if (D == 64)
-    return bf ? launch_fwd_tc<__nv_bfloat16, 64, 3>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
-              : launch_fwd_tc<__half, 64, 3>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
+    return bf ? launch_fwd_tc<__nv_bfloat16, 64, 8>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
+              : launch_fwd_tc<__half, 64, 8>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core forward: head_dim must be 64 or 128");
 }
 

@@ -87,6 +87,37 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// TMA tiled store shared -> global (no reduction); completion tracked with
+// the bulk async-group of the issuing thread.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Per-warpgroup register budget changes (all 4 warps of a warpgroup execute
+// them).  The sum over the CTA must stay within what it was launched with.
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -122,6 +153,17 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t desc_a, uin
       "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16; A is K-major in TMEM (row m
+// in lane m, two consecutive K elements per 32-bit column).
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on `bar` when every tcgen05 async op issued so far by this
 // thread has completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -154,6 +196,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -206,6 +257,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
   const uint32_t chunk = (col >> 3) ^ (row & 7u);
   return row * 128u + chunk * 16u + (col & 7u) * 2u;
+}
+
+// Bits [lo, hi) of a 32-bit word whose bit 0 is column `base` (lo/hi in
+// absolute columns, any range).
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
+  const int a = min(max(lo - base, 0), 32), b = min(max(hi - base, 0), 32);
+  const uint32_t upto_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
+  const uint32_t upto_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+  return upto_b & ~upto_a;
 }
 
 __device__ __forceinline__ float ex2(float x) {
