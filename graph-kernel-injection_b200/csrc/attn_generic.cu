@@ -19,6 +19,8 @@
 // Tiling: forward and dQ use 16 query rows x 64 keys per CTA step (4 warps,
 // 4 rows per warp, lanes over keys for QK^T and over head-dim for PV);
 // dK/dV uses 16 keys x 64 query rows.
+#include <algorithm>
+
 #include "sbfa_common.cuh"
 
 namespace sbfa {
@@ -471,6 +473,21 @@ int dispatch_bwd(int D, const void* q, const void* k, const void* v, const void*
 }
 
 }  // namespace
+
+// Delta = rowsum(O * dO) in fp32 (used by the tensor-core backward too).
+int generic_delta(int dtype, const void* o, const void* dout, float* delta, int64_t rows, int D,
+                  cudaStream_t s) {
+  const int grid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 64);
+  LaunchScope ls("delta_kernel", s);
+  switch (dtype) {
+    case SBFA_F16: delta_kernel<__half><<<grid, 256, 0, s>>>((const __half*)o, (const __half*)dout, delta, rows, D); break;
+    case SBFA_BF16: delta_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, rows, D); break;
+    case SBFA_F32: delta_kernel<float><<<grid, 256, 0, s>>>((const float*)o, (const float*)dout, delta, rows, D); break;
+    case SBFA_F64: delta_kernel<double><<<grid, 256, 0, s>>>((const double*)o, (const double*)dout, delta, rows, D); break;
+    default: return fail(SBFA_ERR_INVALID, "unknown dtype");
+  }
+  return check_launch("delta_kernel");
+}
 
 // Entry points used by capi.cu.
 int generic_tiles(int pass, int64_t* tm, int64_t* tn) {

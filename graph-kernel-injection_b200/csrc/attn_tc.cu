@@ -33,7 +33,7 @@
 #include <mutex>
 #include <type_traits>
 
-#include "tc_prims.cuh"
+#include "tc_attn_common.cuh"
 
 namespace sbfa {
 namespace {
@@ -69,53 +69,6 @@ struct FwdLayout {
   static constexpr uint32_t kBytes = MISC + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;     // room to align the base to 1 KB
 };
-
-__device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, int* status) {
-  // drains our own in-flight async work before exit: ignores the abort flag
-  // but is still bounded
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      record_status(status, kStatusWaitTimeout);
-      return false;
-    }
-  }
-  return true;
-}
-
-// Visibility of the 128 keys [k0, k0+128) for one query row, bit c of
-// vis[c/32] = key k0 + c: sequence end, token rule when causal (at most two
-// intervals: sink and window), lifted block mask on partial tiles.
-__device__ __forceinline__ void row_visibility(uint32_t vis[4], const MaskParams& mp, int row,
-                                               int k0, bool partial) {
-  if (row >= mp.n_q) {
-    vis[0] = vis[1] = vis[2] = vis[3] = 0u;
-    return;
-  }
-  const int end = min(mp.n_kv - k0, kTN);
-  int lo1 = 0, hi1 = end, lo2 = 0, hi2 = 0;
-  if (mp.causal) {
-    const int qpos = mp.q_off + row;
-    const int cend = min(end, qpos - k0 + 1);
-    hi1 = min(cend, mp.sink - k0);
-    lo2 = max(qpos - mp.window + 1 - k0, 0);
-    hi2 = cend;
-  }
-#pragma unroll
-  for (int w = 0; w < 4; ++w) vis[w] = range_bits(lo1, hi1, 32 * w) | range_bits(lo2, hi2, 32 * w);
-  if (partial) {
-    const int32_t* mrow = mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb;
-    const int b0 = k0 / mp.block_n;
-    const int b1 = min((k0 + kTN - 1) / mp.block_n, mp.n_kb - 1);
-    for (int b = b0; b <= b1; ++b) {
-      if (__ldg(mrow + b) != 0) continue;
-      const int lo = b * mp.block_n - k0, hi = lo + mp.block_n;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) vis[w] &= ~range_bits(lo, hi, 32 * w);
-    }
-  }
-}
 
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -306,7 +259,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int k0 = plan_index(ent) * kTN;
       const bool partial = plan_partial(ent);
       uint32_t vis[4];
-      row_visibility(vis, mp, row, k0, partial);
+      row_visibility<kTN>(vis, mp, row, k0, partial);
       ok = __all_sync(0xffffffffu,
                       wait_bar(bar(L::kSFull + x), (uint32_t)(j & 1), abort_flag, status));
       if (!ok) break;
@@ -485,7 +438,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, bool bf16, uint64_t cols, u
 bool tc_supports(int pass, int dtype, int64_t D) {
   if (dtype != SBFA_F16 && dtype != SBFA_BF16) return false;
   if (D != 64 && D != 128) return false;
-  return pass == 0;
+  return pass >= 0 && pass <= 2;
 }
 
 int tc_tiles(int pass, int64_t* tm, int64_t* tn) {
@@ -507,10 +460,5 @@ int tc_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* 
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core forward: head_dim must be 64 or 128");
 }
 
-int tc_bwd(int, int, const void*, const void*, const void*, const void*, const float*,
-           const void*, void*, void*, void*, float*, int, float, const MaskParams&,
-           const int32_t*, const int32_t*, const int32_t*, const int32_t*, int*, cudaStream_t) {
-  return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward not built");
-}
 
 }  // namespace sbfa

@@ -1,0 +1,662 @@
+// Tensor-core backward for sm_100a: separate dK/dV and dQ kernels, both
+// recomputing P from the forward's log-sum-exp (upstream
+// _bwd_dkdv_kernel / _bwd_dq_kernel, sparse_triton_kernel.py:395-601).
+//
+// Both kernels share one structure.  A CTA owns one 128-row tile of the
+// "resident" operand (keys for dK/dV, queries for dQ) and walks the kept
+// tiles of the other operand from the compacted plan (CSC for dK/dV, CSR
+// for dQ).  Every visited 128-wide tile is processed as two 64-wide
+// half-steps u = 2*i + h so that the score tiles S and dP can be double
+// buffered in TMEM:
+//   warp 0       TMA producer (resident tiles once, then a ring of streamed
+//                tile pairs; the dK/dV producer also stages LSE*log2(e) and
+//                Delta of each streamed query tile in shared memory);
+//   warp 1       MMA issuer: S[u%2] and dP[u%2] for half-step u, then, once
+//                the compute group published dS (and P) for u, the
+//                accumulator MMAs, then S/dP for u+2 into the same slot;
+//   warps 4-7    compute group for even half-steps, warps 8-11 for odd
+//                ones: one TMEM lane (row) per thread, 64 score columns per
+//                half-step, P = 2^(S*scale*log2e - LSE*log2e) on visible
+//                pairs, dS = P * (dP - Delta) * scale, packed to 16 bits and
+//                written into the upper half of the slot's TMEM columns,
+//                where the next MMA reads it as the A operand.
+// TMEM (512 columns): S[0] 0-63, S[1] 64-127, dP[0] 128-191, dP[1] 192-255,
+// accumulators from 256 (dV, dK for the dK/dV kernel; dQ for the dQ kernel).
+// Epilogue: accumulators -> 16-bit -> shared memory (128-byte swizzle) -> TMA
+// store; rows past the sequence end are clipped by the tensor map.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "tc_attn_common.cuh"
+
+namespace sbfa {
+namespace {
+
+using namespace tc;
+
+constexpr int kT = 128;        // rows of a resident / streamed tile
+constexpr int kH = 64;         // width of a half-step
+constexpr int kBwdThreads = 384;
+constexpr int kRegsCtl = 64;
+constexpr int kRegsCompute = 208;  // 128*64 + 256*208 <= 384*168
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTS = 0, kTDP = 128, kTAcc = 256;
+
+// ---------------------------------------------------------------------------
+// dK / dV
+// ---------------------------------------------------------------------------
+template <int D, int QST>
+struct DkdvLayout {
+  static constexpr uint32_t kTile = kT * D * 2;
+  static constexpr uint32_t K = 0;
+  static constexpr uint32_t V = K + kTile;
+  static constexpr uint32_t Q0 = V + kTile;                // QST query tiles
+  static constexpr uint32_t DO0 = Q0 + QST * kTile;        // QST dO tiles
+  static constexpr uint32_t LS = DO0 + QST * kTile;        // QST x 128 floats (LSE * log2 e)
+  static constexpr uint32_t DL = LS + QST * kT * 4;        // QST x 128 floats (Delta)
+  static constexpr uint32_t BAR = DL + QST * kT * 4;
+  static constexpr int kKVFull = 0;
+  static constexpr int kQFull = 1;                 // [QST]
+  static constexpr int kQEmpty = 1 + QST;          // [QST]
+  static constexpr int kSFull = 1 + 2 * QST;       // [2]
+  static constexpr int kPFull = 3 + 2 * QST;       // [2]
+  static constexpr int kDone = 5 + 2 * QST;
+  static constexpr int kDrain = 6 + 2 * QST;
+  static constexpr int kNumBars = 7 + 2 * QST;
+  static constexpr uint32_t MISC = BAR + kNumBars * 8;
+  static constexpr uint32_t kAlloc = MISC + 16 + 1024;
+};
+
+template <typename T, int D, int QST>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                   const __grid_constant__ CUtensorMap tmdk,
+                   const __grid_constant__ CUtensorMap tmdv, T* __restrict__ dk,
+                   T* __restrict__ dv, const float* __restrict__ lse,
+                   const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
+                   const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
+                   int* status) {
+  using L = DkdvLayout<D, QST>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kH, false, false);   // M=128 keys, N=64 q
+  constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 keys, N=D
+  constexpr int kBoxes = D / 64;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sb + L::BAR + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // sink-heavy key tiles come first: all heads of key tile 0, then tile 1, ...
+  const int tj = blockIdx.x / BH;
+  const int bh = blockIdx.x % BH;
+  const int e0 = col_ptr[tj];
+  const int nq = col_ptr[tj + 1] - e0;
+  const int U = 2 * nq;
+
+  if (nq == 0) {  // no query sees this key tile: dK = dV = 0
+    for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
+      const int rr = idx / (D / 8), cc = idx % (D / 8);
+      const int key = tj * kT + rr;
+      if (key < mp.n_kv) {
+        const size_t off = ((size_t)bh * mp.n_kv + key) * D;
+        reinterpret_cast<uint4*>(dk + off)[cc] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dv + off)[cc] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::kKVFull), 1);
+    for (int s = 0; s < QST; ++s) {
+      mbar_init(bar(L::kQFull + s), 1);
+      mbar_init(bar(L::kQEmpty + s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar(L::kSFull + x), 1);
+      mbar_init(bar(L::kPFull + x), 128);
+    }
+    mbar_init(bar(L::kDone), 1);
+    mbar_init(bar(L::kDrain), 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    regs_dec<kRegsCtl>();
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        mbar_expect_tx(bar(L::kKVFull), 2 * L::kTile);
+        for (int r = 0; r < kBoxes; ++r) {
+          tma_load_3d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, bh);
+          tma_load_3d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, bh);
+        }
+      }
+      int issued = 0;
+      for (int i = 0; i < nq; ++i) {
+        const int s = i % QST, f = i / QST;
+        if (f > 0) {
+          const bool ok = __all_sync(0xffffffffu, wait_bar(bar(L::kQEmpty + s),
+                                                           (uint32_t)((f - 1) & 1), abort_flag,
+                                                           status));
+          if (!ok) break;
+        }
+        const int ti = plan_index(row_idx[e0 + i]);
+        float* ls = reinterpret_cast<float*>(smem + L::LS) + s * kT;
+        float* dl = reinterpret_cast<float*>(smem + L::DL) + s * kT;
+        for (int rr = lane; rr < kT; rr += 32) {
+          const int row = ti * kT + rr;
+          const bool in = row < mp.n_q;
+          ls[rr] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
+          dl[rr] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_expect_tx(bar(L::kQFull + s), 2 * L::kTile);
+          for (int r = 0; r < kBoxes; ++r) {
+            tma_load_3d(sb + L::Q0 + s * L::kTile + r * 16384u, &tmq, bar(L::kQFull + s), 64 * r,
+                        ti * kT, bh);
+            tma_load_3d(sb + L::DO0 + s * L::kTile + r * 16384u, &tmdo, bar(L::kQFull + s),
+                        64 * r, ti * kT, bh);
+          }
+        }
+        issued = i + 1;
+      }
+      if (lane == 0) {
+        wait_bar_drain(bar(L::kKVFull), 0, status);
+        for (int s = 0; s < QST; ++s) {
+          const int fills = issued > s ? (issued - 1 - s) / QST + 1 : 0;
+          if (fills) wait_bar_drain(bar(L::kQFull + s), (uint32_t)((fills - 1) & 1), status);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      auto issue_sdp = [&](int u) -> bool {
+        const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
+        if (h == 0 &&
+            !wait_bar(bar(L::kQFull + s), (uint32_t)((i / QST) & 1), abort_flag, status))
+          return false;
+        tc_fence_after();
+        const uint32_t qh = sb + L::Q0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t gh = sb + L::DO0 + s * L::kTile + (uint32_t)h * 8192u;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss(tmem + kTS + 64u * slot, desc_kmajor(sb + L::K + off), desc_kmajor(qh + off),
+                     kIdescS, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss(tmem + kTDP + 64u * slot, desc_kmajor(sb + L::V + off), desc_kmajor(gh + off),
+                     kIdescS, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(L::kSFull + slot));
+        return true;
+      };
+      bool ok = wait_bar(bar(L::kKVFull), 0, abort_flag, status);
+      if (ok) ok = issue_sdp(0);
+      if (ok && U > 1) ok = issue_sdp(1);
+      for (int u = 0; ok && u < U; ++u) {
+        const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
+        if (!wait_bar(bar(L::kPFull + slot), (uint32_t)(i & 1), abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t qh = sb + L::Q0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t gh = sb + L::DO0 + s * L::kTile + (uint32_t)h * 8192u;
+#pragma unroll
+        for (int kk = 0; kk < kH / 16; ++kk)  // dV += P^T dO
+          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + 32u + 8u * kk,
+                     desc_mnmajor(gh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     (u > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kH / 16; ++kk)  // dK += dS^T Q
+          mma_f16_ts(tmem + kTAcc + 128u, tmem + kTDP + 64u * slot + 32u + 8u * kk,
+                     desc_mnmajor(qh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     (u > 0 || kk > 0) ? 1u : 0u);
+        if (h == 1) tc_commit(bar(L::kQEmpty + s));
+        if (u + 2 < U) ok = issue_sdp(u + 2);
+      }
+      tc_commit(bar(L::kDone));
+      tc_commit(bar(L::kDrain));
+      wait_bar_drain(bar(L::kDrain), 0, status);
+    }
+  } else {
+    regs_inc<kRegsCompute>();
+    // ------------------------------------------------------------ compute
+    const int grp = (warp - 4) >> 2;  // half-step parity this group serves
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int key = tj * kT + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
+    const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
+    bool ok = true;
+    for (int u = grp; u < U; u += 2) {
+      const int i = u >> 1, s = i % QST;
+      const int32_t ent = row_idx[e0 + i];
+      const int q0 = plan_index(ent) * kT + kH * grp;
+      uint32_t vis[2];
+      col_visibility<kH>(vis, mp, key, q0, plan_partial(ent));
+      ok = __all_sync(0xffffffffu,
+                      wait_bar(bar(L::kSFull + grp), (uint32_t)(i & 1), abort_flag, status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[kH], dpv[kH];
+      tmem_ld32(t_s, sv);
+      tmem_ld32(t_s + 32u, sv + 32);
+      tmem_ld32(t_dp, dpv);
+      tmem_ld32(t_dp + 32u, dpv + 32);
+      tmem_wait_ld();
+      const float* ls = reinterpret_cast<const float*>(smem + L::LS) + s * kT + kH * grp;
+      const float* dl = reinterpret_cast<const float*>(smem + L::DL) + s * kT + kH * grp;
+      uint32_t pk[kH / 2], dk2[kH / 2];
+#pragma unroll
+      for (int c = 0; c < kH / 2; ++c) {
+        float p[2], d[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = 2 * c + e;
+          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
+          p[e] = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - ls[cc]) : 0.f;
+          d[e] = p[e] * (__uint_as_float(dpv[cc]) - dl[cc]) * scale;
+        }
+        pk[c] = pack2<T>(p[0], p[1]);
+        dk2[c] = pack2<T>(d[0], d[1]);
+      }
+      tmem_st32(t_s + 32u, pk);
+      tmem_st32(t_dp + 32u, dk2);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(L::kPFull + grp));
+    }
+    // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes dK
+    // (staged in V's buffer); both buffers are free once every MMA is done
+    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
+    if (ok) {
+      tc_fence_after();
+      const uint32_t t_acc = tmem + lane_base + kTAcc + 128u * grp;
+      const uint32_t stage = sb + (grp == 0 ? L::K : L::V);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(t_acc + 32u * c, t);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int i2 = 0; i2 < 16; ++i2)
+          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]), __uint_as_float(t[2 * i2 + 1]));
+        const uint32_t region = stage + (uint32_t)((32 * c) >> 6) * 16384u;
+#pragma unroll
+        for (int i2 = 0; i2 < 4; ++i2) {
+          const uint32_t addr =
+              region + sw128_offset((uint32_t)r, (uint32_t)((32 * c) & 63) + 8u * i2);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * i2]),
+                       "r"(w[4 * i2 + 1]), "r"(w[4 * i2 + 2]), "r"(w[4 * i2 + 3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1 + grp, 128);
+      if (r == 0) {
+        for (int b = 0; b < kBoxes; ++b)
+          tma_store_3d(grp == 0 ? &tmdv : &tmdk, stage + (uint32_t)b * 16384u, 64 * b, tj * kT,
+                       bh);
+        bulk_commit();
+        bulk_wait_read0();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ
+// ---------------------------------------------------------------------------
+template <int D, int KST>
+struct DqLayout {
+  static constexpr uint32_t kTile = kT * D * 2;
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t DO = Q + kTile;
+  static constexpr uint32_t K0 = DO + kTile;          // KST key tiles
+  static constexpr uint32_t V0 = K0 + KST * kTile;    // KST value tiles
+  static constexpr uint32_t BAR = V0 + KST * kTile;
+  static constexpr int kQFull = 0;
+  static constexpr int kKFull = 1;                 // [KST]
+  static constexpr int kKEmpty = 1 + KST;          // [KST]
+  static constexpr int kSFull = 1 + 2 * KST;       // [2]
+  static constexpr int kPFull = 3 + 2 * KST;       // [2]
+  static constexpr int kDone = 5 + 2 * KST;
+  static constexpr int kDrain = 6 + 2 * KST;
+  static constexpr int kNumBars = 7 + 2 * KST;
+  static constexpr uint32_t MISC = BAR + kNumBars * 8;
+  static constexpr uint32_t kAlloc = MISC + 16 + 1024;
+};
+
+template <typename T, int D, int KST>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                 const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                 const __grid_constant__ CUtensorMap tmdq, T* __restrict__ dq,
+                 const float* __restrict__ lse, const float* __restrict__ delta, float scale,
+                 float scale_log2, MaskParams mp, const int32_t* __restrict__ row_ptr,
+                 const int32_t* __restrict__ col_idx, int* status) {
+  using L = DqLayout<D, KST>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kH, false, false);   // M=128 q, N=64 keys
+  constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 q, N=D
+  constexpr int kBoxes = D / 64;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sb + L::BAR + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ti = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int e0 = row_ptr[ti];
+  const int nk = row_ptr[ti + 1] - e0;
+  const int U = 2 * nk;
+
+  if (nk == 0) {  // the tile's rows see no key: dQ = 0
+    for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
+      const int rr = idx / (D / 8), cc = idx % (D / 8);
+      const int row = ti * kT + rr;
+      if (row < mp.n_q)
+        reinterpret_cast<uint4*>(dq + ((size_t)bh * mp.n_q + row) * D)[cc] =
+            make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::kQFull), 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(bar(L::kKFull + s), 1);
+      mbar_init(bar(L::kKEmpty + s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar(L::kSFull + x), 1);
+      mbar_init(bar(L::kPFull + x), 128);
+    }
+    mbar_init(bar(L::kDone), 1);
+    mbar_init(bar(L::kDrain), 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    regs_dec<kRegsCtl>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      mbar_expect_tx(bar(L::kQFull), 2 * L::kTile);
+      for (int r = 0; r < kBoxes; ++r) {
+        tma_load_3d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, bh);
+        tma_load_3d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, bh);
+      }
+      int issued = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % KST, f = j / KST;
+        if (f > 0 && !wait_bar(bar(L::kKEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status))
+          break;
+        const int kt = plan_index(col_idx[e0 + j]);
+        mbar_expect_tx(bar(L::kKFull + s), 2 * L::kTile);
+        for (int r = 0; r < kBoxes; ++r) {
+          tma_load_3d(sb + L::K0 + s * L::kTile + r * 16384u, &tmk, bar(L::kKFull + s), 64 * r,
+                      kt * kT, bh);
+          tma_load_3d(sb + L::V0 + s * L::kTile + r * 16384u, &tmv, bar(L::kKFull + s), 64 * r,
+                      kt * kT, bh);
+        }
+        issued = j + 1;
+      }
+      wait_bar_drain(bar(L::kQFull), 0, status);
+      for (int s = 0; s < KST; ++s) {
+        const int fills = issued > s ? (issued - 1 - s) / KST + 1 : 0;
+        if (fills) wait_bar_drain(bar(L::kKFull + s), (uint32_t)((fills - 1) & 1), status);
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      auto issue_sdp = [&](int u) -> bool {
+        const int j = u >> 1, h = u & 1, s = j % KST, slot = u & 1;
+        if (h == 0 &&
+            !wait_bar(bar(L::kKFull + s), (uint32_t)((j / KST) & 1), abort_flag, status))
+          return false;
+        tc_fence_after();
+        const uint32_t kh = sb + L::K0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t vh = sb + L::V0 + s * L::kTile + (uint32_t)h * 8192u;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss(tmem + kTS + 64u * slot, desc_kmajor(sb + L::Q + off), desc_kmajor(kh + off),
+                     kIdescS, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss(tmem + kTDP + 64u * slot, desc_kmajor(sb + L::DO + off),
+                     desc_kmajor(vh + off), kIdescS, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(L::kSFull + slot));
+        return true;
+      };
+      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status);
+      if (ok) ok = issue_sdp(0);
+      if (ok && U > 1) ok = issue_sdp(1);
+      for (int u = 0; ok && u < U; ++u) {
+        const int j = u >> 1, h = u & 1, s = j % KST, slot = u & 1;
+        if (!wait_bar(bar(L::kPFull + slot), (uint32_t)(j & 1), abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kh = sb + L::K0 + s * L::kTile + (uint32_t)h * 8192u;
+#pragma unroll
+        for (int kk = 0; kk < kH / 16; ++kk)  // dQ += dS K
+          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + 32u + 8u * kk,
+                     desc_mnmajor(kh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     (u > 0 || kk > 0) ? 1u : 0u);
+        if (h == 1) tc_commit(bar(L::kKEmpty + s));
+        if (u + 2 < U) ok = issue_sdp(u + 2);
+      }
+      tc_commit(bar(L::kDone));
+      tc_commit(bar(L::kDrain));
+      wait_bar_drain(bar(L::kDrain), 0, status);
+    }
+  } else {
+    regs_inc<kRegsCompute>();
+    // ------------------------------------------------------------ compute
+    const int grp = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int row = ti * kT + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
+    const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
+    const bool in = row < mp.n_q;
+    const float lse2 = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
+    const float dl = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
+    bool ok = true;
+    for (int u = grp; u < U; u += 2) {
+      const int j = u >> 1;
+      const int32_t ent = col_idx[e0 + j];
+      const int k0 = plan_index(ent) * kT + kH * grp;
+      uint32_t vis[2];
+      row_visibility<kH>(vis, mp, row, k0, plan_partial(ent));
+      ok = __all_sync(0xffffffffu,
+                      wait_bar(bar(L::kSFull + grp), (uint32_t)(j & 1), abort_flag, status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[kH], dpv[kH];
+      tmem_ld32(t_s, sv);
+      tmem_ld32(t_s + 32u, sv + 32);
+      tmem_ld32(t_dp, dpv);
+      tmem_ld32(t_dp + 32u, dpv + 32);
+      tmem_wait_ld();
+      uint32_t ds2[kH / 2];
+#pragma unroll
+      for (int c = 0; c < kH / 2; ++c) {
+        float d[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = 2 * c + e;
+          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
+          const float p = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lse2) : 0.f;
+          d[e] = p * (__uint_as_float(dpv[cc]) - dl) * scale;
+        }
+        ds2[c] = pack2<T>(d[0], d[1]);
+      }
+      tmem_st32(t_s + 32u, ds2);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(L::kPFull + grp));
+    }
+    // epilogue: dQ columns [64*grp, 64*grp + 64) staged in Q's buffer
+    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
+    if (ok && 64 * grp < D) {
+      tc_fence_after();
+      const uint32_t t_acc = tmem + lane_base + kTAcc + 64u * grp;
+      const uint32_t region = sb + L::Q + (uint32_t)grp * 16384u;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t t[32];
+        tmem_ld32(t_acc + 32u * c, t);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int i2 = 0; i2 < 16; ++i2)
+          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]), __uint_as_float(t[2 * i2 + 1]));
+#pragma unroll
+        for (int i2 = 0; i2 < 4; ++i2) {
+          const uint32_t addr = region + sw128_offset((uint32_t)r, 32u * c + 8u * i2);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * i2]),
+                       "r"(w[4 * i2 + 1]), "r"(w[4 * i2 + 2]), "r"(w[4 * i2 + 3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1 + grp, 128);
+      if (r == 0) {
+        tma_store_3d(&tmdq, region, 64 * grp, ti * kT, bh);
+        bulk_commit();
+        bulk_wait_read0();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, int D, int QST, int KST>
+int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
+                  void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
+                  const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
+                  const int32_t* kv_cp, const int32_t* kv_ri, int* status, cudaStream_t s) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
+  const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv, bh = (uint64_t)BH;
+  if (int rc = make_tmap_3d(&mq, q, kBF16, D, nq, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mdo, dout, kBF16, D, nq, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mk, k, kBF16, D, nkv, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mv, v, kBF16, D, nkv, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mdq, dq, kBF16, D, nq, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mdk, dk, kBF16, D, nkv, bh, kT)) return rc;
+  if (int rc = make_tmap_3d(&mdv, dv, kBF16, D, nkv, bh, kT)) return rc;
+  const float sl = scale * kLog2e;
+  {
+    using L = DkdvLayout<D, QST>;
+    auto kern = dkdv_tc_kernel<T, D, QST>;
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)L::kAlloc),
+                            "cudaFuncSetAttribute(dkdv_tc)"))
+      return rc;
+    const int n_tj = ceil_div_i(mp.n_kv, kT);
+    LaunchScope ls("dkdv_tc_kernel", s);
+    kern<<<n_tj * BH, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse,
+                                                  delta, scale, sl, mp, kv_cp, kv_ri, BH, status);
+  }
+  if (int rc = check_launch("dkdv_tc_kernel")) return rc;
+  {
+    using L = DqLayout<D, KST>;
+    auto kern = dq_tc_kernel<T, D, KST>;
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)L::kAlloc),
+                            "cudaFuncSetAttribute(dq_tc)"))
+      return rc;
+    dim3 grid(ceil_div_i(mp.n_q, kT), BH);
+    LaunchScope ls("dq_tc_kernel", s);
+    kern<<<grid, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdq, (T*)dq, lse, delta, scale, sl,
+                                              mp, dq_rp, dq_ci, status);
+  }
+  return check_launch("dq_tc_kernel");
+}
+
+}  // namespace
+
+int generic_delta(int dtype, const void* o, const void* dout, float* delta, int64_t rows, int D,
+                  cudaStream_t s);
+
+int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
+           const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta, int BH,
+           float scale, const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
+           const int32_t* kv_cp, const int32_t* kv_ri, int* status, cudaStream_t s) {
+  if (int rc = generic_delta(dtype, o, dout, delta, (int64_t)BH * mp.n_q, D, s)) return rc;
+  const bool bf = dtype == SBFA_BF16;
+  if (D == 128)
+    return bf ? launch_bwd_tc<__nv_bfloat16, 128, 2, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+                                                        scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
+                                                        status, s)
+              : launch_bwd_tc<__half, 128, 2, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+                                                 mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
+  if (D == 64)
+    return bf ? launch_bwd_tc<__nv_bfloat16, 64, 4, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+                                                       scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
+                                                       status, s)
+              : launch_bwd_tc<__half, 64, 4, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+                                                mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
+  return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward: head_dim must be 64 or 128");
+}
+
+}  // namespace sbfa

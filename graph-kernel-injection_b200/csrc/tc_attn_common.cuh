@@ -1,0 +1,97 @@
+// Pieces shared by the tensor-core attention kernels (forward, dQ, dK/dV):
+// the drain wait used before exit and the per-thread visibility masks.
+#pragma once
+
+#include "tc_prims.cuh"
+
+namespace sbfa {
+namespace tc {
+
+__device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, int* status) {
+  // drains our own in-flight async work before exit: ignores the abort flag
+  // but is still bounded
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      record_status(status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Visibility of the NCOL keys [k0, k0+NCOL) for one query row, bit c of
+// vis[c/32] = key k0 + c: sequence end, token rule when causal (at most two
+// intervals: sink and window), lifted block mask on partial tiles.
+template <int NCOL>
+__device__ __forceinline__ void row_visibility(uint32_t (&vis)[NCOL / 32], const MaskParams& mp,
+                                               int row, int k0, bool partial) {
+  constexpr int W = NCOL / 32;
+  if (row >= mp.n_q) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) vis[w] = 0u;
+    return;
+  }
+  const int end = min(mp.n_kv - k0, NCOL);
+  int lo1 = 0, hi1 = end, lo2 = 0, hi2 = 0;
+  if (mp.causal) {
+    const int qpos = mp.q_off + row;
+    const int cend = min(end, qpos - k0 + 1);
+    hi1 = min(cend, mp.sink - k0);
+    lo2 = max(qpos - mp.window + 1 - k0, 0);
+    hi2 = cend;
+  }
+#pragma unroll
+  for (int w = 0; w < W; ++w) vis[w] = range_bits(lo1, hi1, 32 * w) | range_bits(lo2, hi2, 32 * w);
+  if (partial) {
+    const int32_t* mrow = mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb;
+    const int b0 = k0 / mp.block_n;
+    const int b1 = min((k0 + NCOL - 1) / mp.block_n, mp.n_kb - 1);
+    for (int b = b0; b <= b1; ++b) {
+      if (__ldg(mrow + b) != 0) continue;
+      const int lo = b * mp.block_n - k0, hi = lo + mp.block_n;
+#pragma unroll
+      for (int w = 0; w < W; ++w) vis[w] &= ~range_bits(lo, hi, 32 * w);
+    }
+  }
+}
+
+
+// Visibility of the NROW query rows [q0, q0+NROW) for one key, bit c of
+// vis[c/32] = row q0 + c (the column view used by the dK/dV kernel): for a
+// fixed key the visible rows form one interval (causal lower end, window
+// upper end unless the key is a sink), cut by the lifted block mask.
+template <int NROW>
+__device__ __forceinline__ void col_visibility(uint32_t (&vis)[NROW / 32], const MaskParams& mp,
+                                               int key, int q0, bool partial) {
+  constexpr int W = NROW / 32;
+  if (key >= mp.n_kv) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) vis[w] = 0u;
+    return;
+  }
+  const int end = min(mp.n_q - q0, NROW);
+  int lo = 0, hi = end;
+  if (mp.causal) {
+    lo = max(key - mp.q_off - q0, 0);                       // q >= key
+    if (key >= mp.sink) hi = min(end, key + mp.window - mp.q_off - q0);  // q <= key + W - 1
+  }
+#pragma unroll
+  for (int w = 0; w < W; ++w) vis[w] = range_bits(lo, hi, 32 * w);
+  if (partial) {
+    const int kb = key / mp.block_n;
+    const int b0 = q0 / mp.block_m;
+    const int b1 = (q0 + NROW - 1) / mp.block_m;
+    const int nqb = (mp.n_q + mp.block_m - 1) / mp.block_m;
+    for (int b = b0; b <= min(b1, nqb - 1); ++b) {
+      if (__ldg(mp.block_mask + (size_t)b * mp.n_kb + kb) != 0) continue;
+      const int rlo = b * mp.block_m - q0, rhi = rlo + mp.block_m;
+#pragma unroll
+      for (int w = 0; w < W; ++w) vis[w] &= ~range_bits(rlo, rhi, 32 * w);
+    }
+  }
+}
+
+}  // namespace tc
+}  // namespace sbfa
