@@ -147,8 +147,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                       row0 + x * kTM, bh);
       int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
       bool ok = true;
+      int next_ent = col_idx[e0];
       for (int j = 0; ok && j < n; ++j) {
-        const int kt = plan_index(col_idx[e0 + j]);
+        const int kt = plan_index(next_ent);
+        if (j + 1 < n) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
         for (int part = 0; part < 2; ++part) {
           const int e = 2 * j + part;
           const int s = e % STAGES, f = e / STAGES;

@@ -14,12 +14,14 @@
 //   warp 1       MMA issuer: S[u%2] and dP[u%2] for half-step u, then, once
 //                the compute group published dS (and P) for u, the
 //                accumulator MMAs, then S/dP for u+2 into the same slot;
-//   warps 4-7    compute group for even half-steps, warps 8-11 for odd
-//                ones: one TMEM lane (row) per thread, 64 score columns per
-//                half-step, P = 2^(S*scale*log2e - LSE*log2e) on visible
-//                pairs, dS = P * (dP - Delta) * scale, packed to 16 bits and
-//                written into the upper half of the slot's TMEM columns,
-//                where the next MMA reads it as the A operand.
+//   warps 4-11   two compute groups that both work on every half-step:
+//                one TMEM lane (row) per thread, group g takes score columns
+//                [32g, 32g+32) of the half-step, computes
+//                P = 2^(S*scale*log2e - LSE*log2e) on visible pairs and
+//                dS = P * (dP - Delta) * scale, packs them to 16 bits and
+//                writes them over the first 16 of the 32 TMEM columns it just
+//                read (so the groups never touch each other's inputs); the
+//                accumulator MMAs read them there as the A operand.
 // TMEM (512 columns): S[0] 0-63, S[1] 64-127, dP[0] 128-191, dP[1] 192-255,
 // accumulators from 256 (dV, dK for the dK/dV kernel; dQ for the dQ kernel).
 // Epilogue: accumulators -> 16-bit -> shared memory (128-byte swizzle) -> TMA
@@ -45,6 +47,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTS = 0, kTDP = 128, kTAcc = 256;
 
+// TMEM column (within a 64-column slot) of the packed 16-bit A operand for
+// k-step kk of an accumulator MMA: compute group g stores its 32 score
+// columns, packed, at slot columns [32g, 32g+16).
+__device__ __forceinline__ uint32_t a_col(int kk) {
+  return 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
+}
+
 // ---------------------------------------------------------------------------
 // dK / dV
 // ---------------------------------------------------------------------------
@@ -65,7 +74,8 @@ struct DkdvLayout {
   static constexpr int kPFull = 3 + 2 * QST;       // [2]
   static constexpr int kDone = 5 + 2 * QST;
   static constexpr int kDrain = 6 + 2 * QST;
-  static constexpr int kNumBars = 7 + 2 * QST;
+  static constexpr int kLFull = 7 + 2 * QST;       // [QST] LSE/Delta staged
+  static constexpr int kNumBars = 7 + 3 * QST;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kAlloc = MISC + 16 + 1024;
 };
@@ -120,10 +130,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int s = 0; s < QST; ++s) {
       mbar_init(bar(L::kQFull + s), 1);
       mbar_init(bar(L::kQEmpty + s), 1);
+      mbar_init(bar(L::kLFull + s), 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(L::kSFull + x), 1);
-      mbar_init(bar(L::kPFull + x), 128);
+      mbar_init(bar(L::kPFull + x), 256);
     }
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
@@ -151,24 +162,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       int issued = 0;
+      int next_ent = row_idx[e0];
       for (int i = 0; i < nq; ++i) {
         const int s = i % QST, f = i / QST;
+        const int ti = plan_index(next_ent);
+        if (i + 1 < nq) next_ent = row_idx[e0 + i + 1];  // prefetch the next plan entry
         if (f > 0) {
           const bool ok = __all_sync(0xffffffffu, wait_bar(bar(L::kQEmpty + s),
                                                            (uint32_t)((f - 1) & 1), abort_flag,
                                                            status));
           if (!ok) break;
         }
-        const int ti = plan_index(row_idx[e0 + i]);
-        float* ls = reinterpret_cast<float*>(smem + L::LS) + s * kT;
-        float* dl = reinterpret_cast<float*>(smem + L::DL) + s * kT;
-        for (int rr = lane; rr < kT; rr += 32) {
-          const int row = ti * kT + rr;
-          const bool in = row < mp.n_q;
-          ls[rr] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
-          dl[rr] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
-        }
-        __syncwarp();
+        // tensor copies first: the MMA warp only needs Q and dO
         if (lane == 0) {
           mbar_expect_tx(bar(L::kQFull + s), 2 * L::kTile);
           for (int r = 0; r < kBoxes; ++r) {
@@ -179,6 +184,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
         issued = i + 1;
+        // then the per-row LSE (log2 units) and Delta for the compute groups
+        float* ls = reinterpret_cast<float*>(smem + L::LS) + s * kT;
+        float* dl = reinterpret_cast<float*>(smem + L::DL) + s * kT;
+        for (int rr = lane; rr < kT; rr += 32) {
+          const int row = ti * kT + rr;
+          const bool in = row < mp.n_q;
+          ls[rr] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
+          dl[rr] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::kLFull + s));
       }
       if (lane == 0) {
         wait_bar_drain(bar(L::kKVFull), 0, status);
@@ -226,12 +242,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t gh = sb + L::DO0 + s * L::kTile + (uint32_t)h * 8192u;
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dV += P^T dO
-          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + 32u + 8u * kk,
+          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
                      desc_mnmajor(gh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dK += dS^T Q
-          mma_f16_ts(tmem + kTAcc + 128u, tmem + kTDP + 64u * slot + 32u + 8u * kk,
+          mma_f16_ts(tmem + kTAcc + 128u, tmem + kTDP + 64u * slot + a_col(kk),
                      desc_mnmajor(qh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
         if (h == 1) tc_commit(bar(L::kQEmpty + s));
@@ -244,51 +260,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     regs_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 4) >> 2;  // half-step parity this group serves
+    const int grp = (warp - 4) >> 2;  // column half of every half-step this group takes
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int key = tj * kT + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
-    const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
     bool ok = true;
-    for (int u = grp; u < U; u += 2) {
-      const int i = u >> 1, s = i % QST;
+    for (int u = 0; u < U; ++u) {
+      const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
       const int32_t ent = row_idx[e0 + i];
-      const int q0 = plan_index(ent) * kT + kH * grp;
-      uint32_t vis[2];
-      col_visibility<kH>(vis, mp, key, q0, plan_partial(ent));
+      const int c0 = kH * h + 32 * grp;  // first of this group's 32 query columns in the tile
+      uint32_t vis[1];
+      col_visibility<32>(vis, mp, key, plan_index(ent) * kT + c0, plan_partial(ent));
       ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kSFull + grp), (uint32_t)(i & 1), abort_flag, status));
+                      wait_bar(bar(L::kLFull + s), (uint32_t)((i / QST) & 1), abort_flag, status) &&
+                          wait_bar(bar(L::kSFull + slot), (uint32_t)(i & 1), abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kH], dpv[kH];
+      const uint32_t t_s = tmem + lane_base + kTS + 64u * slot + 32u * grp;
+      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * slot + 32u * grp;
+      uint32_t sv[32], dpv[32];
       tmem_ld32(t_s, sv);
-      tmem_ld32(t_s + 32u, sv + 32);
       tmem_ld32(t_dp, dpv);
-      tmem_ld32(t_dp + 32u, dpv + 32);
       tmem_wait_ld();
-      const float* ls = reinterpret_cast<const float*>(smem + L::LS) + s * kT + kH * grp;
-      const float* dl = reinterpret_cast<const float*>(smem + L::DL) + s * kT + kH * grp;
-      uint32_t pk[kH / 2], dk2[kH / 2];
+      const float4* ls4 = reinterpret_cast<const float4*>(smem + L::LS) + (s * kT + c0) / 4;
+      const float4* dl4 = reinterpret_cast<const float4*>(smem + L::DL) + (s * kT + c0) / 4;
+      uint32_t pk[16], dk2[16];
 #pragma unroll
-      for (int c = 0; c < kH / 2; ++c) {
-        float p[2], d[2];
+      for (int q4 = 0; q4 < 8; ++q4) {
+        const float4 l4 = ls4[q4], d4 = dl4[q4];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float p[4], d[4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e;
-          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
-          p[e] = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - ls[cc]) : 0.f;
-          d[e] = p[e] * (__uint_as_float(dpv[cc]) - dl[cc]) * scale;
+        for (int e = 0; e < 4; ++e) {
+          const int cc = 4 * q4 + e;
+          const bool on = (vis[0] >> cc) & 1u;
+          p[e] = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lv[e]) : 0.f;
+          d[e] = p[e] * (__uint_as_float(dpv[cc]) - dv4[e]) * scale;
         }
-        pk[c] = pack2<T>(p[0], p[1]);
-        dk2[c] = pack2<T>(d[0], d[1]);
+        pk[2 * q4] = pack2<T>(p[0], p[1]);
+        pk[2 * q4 + 1] = pack2<T>(p[2], p[3]);
+        dk2[2 * q4] = pack2<T>(d[0], d[1]);
+        dk2[2 * q4 + 1] = pack2<T>(d[2], d[3]);
       }
-      tmem_st32(t_s + 32u, pk);
-      tmem_st32(t_dp + 32u, dk2);
+      tmem_st16(t_s, pk);
+      tmem_st16(t_dp, dk2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull + grp));
+      mbar_arrive(bar(L::kPFull + slot));
     }
     // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes dK
     // (staged in V's buffer); both buffers are free once every MMA is done
@@ -407,7 +426,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(L::kSFull + x), 1);
-      mbar_init(bar(L::kPFull + x), 128);
+      mbar_init(bar(L::kPFull + x), 256);
     }
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
@@ -433,11 +452,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_3d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, bh);
       }
       int issued = 0;
+      int next_ent = col_idx[e0];
       for (int j = 0; j < nk; ++j) {
         const int s = j % KST, f = j / KST;
+        const int kt = plan_index(next_ent);
+        if (j + 1 < nk) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
         if (f > 0 && !wait_bar(bar(L::kKEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status))
           break;
-        const int kt = plan_index(col_idx[e0 + j]);
         mbar_expect_tx(bar(L::kKFull + s), 2 * L::kTile);
         for (int r = 0; r < kBoxes; ++r) {
           tma_load_3d(sb + L::K0 + s * L::kTile + r * 16384u, &tmk, bar(L::kKFull + s), 64 * r,
@@ -490,7 +511,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t kh = sb + L::K0 + s * L::kTile + (uint32_t)h * 8192u;
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dQ += dS K
-          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + 32u + 8u * kk,
+          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
                      desc_mnmajor(kh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
         if (h == 1) tc_commit(bar(L::kKEmpty + s));
@@ -503,50 +524,48 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     regs_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 4) >> 2;
+    const int grp = (warp - 4) >> 2;  // column half of every half-step this group takes
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int row = ti * kT + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
-    const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
     const bool in = row < mp.n_q;
     const float lse2 = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
     const float dl = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
     bool ok = true;
-    for (int u = grp; u < U; u += 2) {
-      const int j = u >> 1;
+    for (int u = 0; u < U; ++u) {
+      const int j = u >> 1, h = u & 1, slot = u & 1;
       const int32_t ent = col_idx[e0 + j];
-      const int k0 = plan_index(ent) * kT + kH * grp;
-      uint32_t vis[2];
-      row_visibility<kH>(vis, mp, row, k0, plan_partial(ent));
+      uint32_t vis[1];
+      row_visibility<32>(vis, mp, row, plan_index(ent) * kT + kH * h + 32 * grp,
+                         plan_partial(ent));
       ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kSFull + grp), (uint32_t)(j & 1), abort_flag, status));
+                      wait_bar(bar(L::kSFull + slot), (uint32_t)(j & 1), abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kH], dpv[kH];
+      const uint32_t t_s = tmem + lane_base + kTS + 64u * slot + 32u * grp;
+      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * slot + 32u * grp;
+      uint32_t sv[32], dpv[32];
       tmem_ld32(t_s, sv);
-      tmem_ld32(t_s + 32u, sv + 32);
       tmem_ld32(t_dp, dpv);
-      tmem_ld32(t_dp + 32u, dpv + 32);
       tmem_wait_ld();
-      uint32_t ds2[kH / 2];
+      uint32_t ds2[16];
 #pragma unroll
-      for (int c = 0; c < kH / 2; ++c) {
+      for (int c = 0; c < 16; ++c) {
         float d[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int cc = 2 * c + e;
-          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
+          const bool on = (vis[0] >> cc) & 1u;
           const float p = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lse2) : 0.f;
           d[e] = p * (__uint_as_float(dpv[cc]) - dl) * scale;
         }
         ds2[c] = pack2<T>(d[0], d[1]);
       }
-      tmem_st32(t_s + 32u, ds2);
+      tmem_st16(t_s, ds2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull + grp));
+      mbar_arrive(bar(L::kPFull + slot));
     }
     // epilogue: dQ columns [64*grp, 64*grp + 64) staged in Q's buffer
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
