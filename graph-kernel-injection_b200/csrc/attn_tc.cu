@@ -178,23 +178,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         return wait_bar(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
                         status);
       };
+      // base descriptors, built once; MMAs add constant offsets
+      const uint64_t dq0 = desc_kmajor(sb + L::Q);
+      const uint64_t dkv_k = desc_kmajor(sb + L::KV);
+      const uint64_t dkv_v = desc_mnmajor(sb + L::KV, 16384u);
       auto qk = [&](int x, int e) {
-        const uint32_t kbase = sb + L::KV + (uint32_t)(e % STAGES) * L::kTile;
-        const uint32_t qbase = sb + L::Q + (uint32_t)x * L::kTile;
+        const uint64_t dq = desc_advance(dq0, (uint32_t)x * L::kTile);
+        const uint64_t dk = desc_advance(dkv_k, (uint32_t)(e % STAGES) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + 128u * x, desc_kmajor(qbase + off), desc_kmajor(kbase + off), kIdescQK,
+          mma_f16_ss(tmem + 128u * x, desc_advance(dq, off), desc_advance(dk, off), kIdescQK,
                      kk > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int x, int e, bool acc) {
-        const uint32_t vbase = sb + L::KV + (uint32_t)(e % STAGES) * L::kTile;
+        const uint64_t dv = desc_advance(dkv_v, (uint32_t)(e % STAGES) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < kTN / 16; ++kk)
           mma_f16_ts(tmem + 256u + 128u * x, tmem + 128u * x + 64u + 8u * kk,
-                     desc_mnmajor(vbase + (uint32_t)kk * 2048u, 16384u), kIdescPV,
-                     (acc || kk > 0) ? 1u : 0u);
+                     desc_advance(dv, (uint32_t)kk * 2048u), kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status) && kv_wait(0);
       if (ok) {

@@ -205,24 +205,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
+      // base descriptors, built once; MMAs add constant offsets
+      const uint64_t d_k = desc_kmajor(sb + L::K), d_v = desc_kmajor(sb + L::V);
+      const uint64_t d_q0 = desc_kmajor(sb + L::Q0), d_g0 = desc_kmajor(sb + L::DO0);
+      const uint64_t m_q0 = desc_mnmajor(sb + L::Q0, 16384u);
+      const uint64_t m_g0 = desc_mnmajor(sb + L::DO0, 16384u);
       auto issue_sdp = [&](int u) -> bool {
         const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
         if (h == 0 &&
             !wait_bar(bar(L::kQFull + s), (uint32_t)((i / QST) & 1), abort_flag, status))
           return false;
         tc_fence_after();
-        const uint32_t qh = sb + L::Q0 + s * L::kTile + (uint32_t)h * 8192u;
-        const uint32_t gh = sb + L::DO0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
+        const uint64_t dq = desc_advance(d_q0, half), dg = desc_advance(d_g0, half);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTS + 64u * slot, desc_kmajor(sb + L::K + off), desc_kmajor(qh + off),
+          mma_f16_ss(tmem + kTS + 64u * slot, desc_advance(d_k, off), desc_advance(dq, off),
                      kIdescS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTDP + 64u * slot, desc_kmajor(sb + L::V + off), desc_kmajor(gh + off),
+          mma_f16_ss(tmem + kTDP + 64u * slot, desc_advance(d_v, off), desc_advance(dg, off),
                      kIdescS, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(L::kSFull + slot));
@@ -238,17 +243,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t qh = sb + L::Q0 + s * L::kTile + (uint32_t)h * 8192u;
-        const uint32_t gh = sb + L::DO0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
+        const uint64_t mg = desc_advance(m_g0, half), mq = desc_advance(m_q0, half);
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dV += P^T dO
           mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
-                     desc_mnmajor(gh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     desc_advance(mg, (uint32_t)kk * 2048u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dK += dS^T Q
           mma_f16_ts(tmem + kTAcc + 128u, tmem + kTDP + 64u * slot + a_col(kk),
-                     desc_mnmajor(qh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     desc_advance(mq, (uint32_t)kk * 2048u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
         if (h == 1) tc_commit(bar(L::kQEmpty + s));
         if (u + 2 < U) ok = issue_sdp(u + 2);
@@ -475,25 +480,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
+      // base descriptors, built once; MMAs add constant offsets
+      const uint64_t d_q = desc_kmajor(sb + L::Q), d_g = desc_kmajor(sb + L::DO);
+      const uint64_t d_k0 = desc_kmajor(sb + L::K0), d_v0 = desc_kmajor(sb + L::V0);
+      const uint64_t m_k0 = desc_mnmajor(sb + L::K0, 16384u);
       auto issue_sdp = [&](int u) -> bool {
         const int j = u >> 1, h = u & 1, s = j % KST, slot = u & 1;
         if (h == 0 &&
             !wait_bar(bar(L::kKFull + s), (uint32_t)((j / KST) & 1), abort_flag, status))
           return false;
         tc_fence_after();
-        const uint32_t kh = sb + L::K0 + s * L::kTile + (uint32_t)h * 8192u;
-        const uint32_t vh = sb + L::V0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
+        const uint64_t dk = desc_advance(d_k0, half), dv = desc_advance(d_v0, half);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTS + 64u * slot, desc_kmajor(sb + L::Q + off), desc_kmajor(kh + off),
+          mma_f16_ss(tmem + kTS + 64u * slot, desc_advance(d_q, off), desc_advance(dk, off),
                      kIdescS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTDP + 64u * slot, desc_kmajor(sb + L::DO + off),
-                     desc_kmajor(vh + off), kIdescS, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + kTDP + 64u * slot, desc_advance(d_g, off), desc_advance(dv, off),
+                     kIdescS, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(L::kSFull + slot));
         return true;
@@ -508,11 +517,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t kh = sb + L::K0 + s * L::kTile + (uint32_t)h * 8192u;
+        const uint64_t mk = desc_advance(m_k0, s * L::kTile + (uint32_t)h * 8192u);
 #pragma unroll
         for (int kk = 0; kk < kH / 16; ++kk)  // dQ += dS K
           mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
-                     desc_mnmajor(kh + (uint32_t)kk * 2048u, 16384u), kIdescAcc,
+                     desc_advance(mk, (uint32_t)kk * 2048u), kIdescAcc,
                      (u > 0 || kk > 0) ? 1u : 0u);
         if (h == 1) tc_commit(bar(L::kKEmpty + s));
         if (u + 2 < U) ok = issue_sdp(u + 2);

@@ -9,7 +9,7 @@
 
 #include <string>
 
-#include "../../include/sbfa.h"
+#include "sbfa.h"
 
 namespace sbfa {
 

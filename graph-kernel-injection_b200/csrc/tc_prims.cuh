@@ -233,6 +233,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_
   d |= (uint64_t)2 << 61;  // SWIZZLE_128B
   return d;
 }
+// The start-address field is the low 14 bits of (address >> 4), so for
+// offsets that keep the address inside shared memory
+//   desc(addr + off) == desc(addr) + (off >> 4):
+// kernels build one base descriptor per buffer and add constant offsets.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t off_bytes) {
+  return desc + (uint64_t)(off_bytes >> 4);
+}
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
   return smem_desc_sw128(addr, 16, 1024);
 }
