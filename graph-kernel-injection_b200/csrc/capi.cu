@@ -26,6 +26,7 @@ int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, c
                 const int32_t* c, const int32_t* d, cudaStream_t s);
 // decode.cu
 int decode_tile();
+int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t window);
 int decode_group(int dtype, int64_t D);
 int decode_nsplit(int64_t BH, int64_t est_tiles);
 int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit);
@@ -304,15 +305,6 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
                      softmax_scale, mp, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx, s);
 }
 
-namespace {
-int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t window) {
-  const int64_t t = decode_tile();
-  const int64_t all = (n_kv + t - 1) / t;
-  if (!is_causal) return all;
-  const int64_t vis = std::min<int64_t>(n_kv, sink) + std::min<int64_t>(n_kv, window);
-  return std::min<int64_t>(all, (vis + t - 1) / t + 2);
-}
-}  // namespace
 
 extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
                                                int64_t head_dim, int64_t block_n) {

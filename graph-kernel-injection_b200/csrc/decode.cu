@@ -17,6 +17,7 @@
 //    directly (one split) or a partial to the workspace, merged by
 //    decode_merge_kernel (several splits).
 #include <algorithm>
+#include <mutex>
 
 #include "sbfa_common.cuh"
 
@@ -243,6 +244,17 @@ int dispatch_decode(int G, const void* q, const void* k, const void* v, void* o,
 
 int decode_tile() { return kDecTile; }
 
+// Kept tiles the decode query can touch: every tile when the block mask is
+// the only limit, else the tiles holding the sink and window keys (+2 for
+// boundary tiles).
+int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t window) {
+  const int64_t t = kDecTile;
+  const int64_t all = (n_kv + t - 1) / t;
+  if (!is_causal) return all;
+  const int64_t vis = std::min<int64_t>(n_kv, sink) + std::min<int64_t>(n_kv, window);
+  return std::min<int64_t>(all, (vis + t - 1) / t + 2);
+}
+
 // Lanes per key row, or 0 when the head dim does not map onto 16-byte
 // vectors (the caller then uses the generic forward).
 int decode_group(int dtype, int64_t D) {
@@ -282,3 +294,75 @@ int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, 
 }
 
 }  // namespace sbfa
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode
+// ---------------------------------------------------------------------------
+// Scratch for sbfa_decode_noalloc: the decode plan (row_ptr, col_idx, nnz)
+// followed by the split-KV partials.  A file-scope device array, so every
+// GPU that loads libsbfa holds these bytes until the process exits.
+namespace sbfa {
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+std::mutex g_scratch_mu;
+unsigned char* g_scratch_addr[64] = {nullptr};
+
+// Device address of g_decode_scratch on the current device, resolved once
+// per device (the host-side symbol is only a stand-in and must never be
+// handed to a kernel).
+int scratch_base(unsigned char** out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(SBFA_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_decode_scratch),
+                            "cudaGetSymbolAddress(decode scratch)"))
+      return rc;
+    g_scratch_addr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return SBFA_OK;
+}
+}  // namespace
+}  // namespace sbfa
+
+extern "C" int sbfa_decode_noalloc(const void* q, const void* k, const void* v, void* o,
+                                   float* lse, int64_t B, int64_t H, int64_t n_kv,
+                                   int64_t head_dim, int dtype, double softmax_scale,
+                                   int is_causal, int64_t sink, int64_t window,
+                                   const int32_t* block_mask, int64_t block_m, int64_t block_n,
+                                   void* stream) {
+  using namespace sbfa;
+  if (B <= 0 || H <= 0 || n_kv <= 0 || head_dim <= 0)
+    return fail(SBFA_ERR_INVALID, "B, H, n_kv and head_dim must be positive");
+  if (sink < 0 || window < 0)
+    return fail(SBFA_ERR_INVALID, "sink_size and window_size must be non-negative");
+  const int64_t n_tiles = (n_kv + kDecTile - 1) / kDecTile;
+  // plan: row_ptr[2], col_idx[n_tiles], nnz[1]; partials start on a 256-byte boundary
+  const int64_t plan_bytes = ((2 + n_tiles + 1) * (int64_t)sizeof(int32_t) + 255) / 256 * 256;
+  const int ns = decode_nsplit(B * H, decode_est_tiles(n_kv, is_causal, sink, window));
+  const int64_t ws_bytes = decode_ws_bytes(B * H, head_dim, ns);
+  if (plan_bytes + ws_bytes > (int64_t)kNoAllocScratchBytes)
+    return fail(SBFA_ERR_INVALID,
+                "sbfa_decode_noalloc: this shape needs " + std::to_string(plan_bytes + ws_bytes) +
+                    " bytes of scratch, more than the static " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    "-byte buffer; use sbfa_decode with a caller-provided workspace");
+  unsigned char* base = nullptr;
+  if (int rc = scratch_base(&base)) return rc;
+  int32_t* row_ptr = reinterpret_cast<int32_t*>(base);
+  int32_t* col_idx = row_ptr + 2;
+  int32_t* nnz = col_idx + n_tiles;
+  // every scratch byte read below is written first in stream order: the plan
+  // kernels write row_ptr (scan sets row_ptr[0] = 0) and the kept col_idx
+  // entries; each split writes its whole partial record before the merge
+  if (int rc = sbfa_build_plan(block_mask, 1, n_kv, block_m, block_n, 1, kDecTile, row_ptr,
+                               col_idx, nullptr, nullptr, nnz, stream))
+    return rc;
+  return sbfa_decode(q, k, v, o, lse, B, H, n_kv, head_dim, dtype, softmax_scale, is_causal, sink,
+                     window, block_mask, block_m, block_n, row_ptr, col_idx,
+                     ws_bytes > 0 ? base + plan_bytes : nullptr, ws_bytes, stream);
+}

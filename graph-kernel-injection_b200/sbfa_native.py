@@ -51,6 +51,8 @@ _SIGNATURES = {
                      _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _i32),
     "sbfa_decode_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "sbfa_decode_supported": ([_i32, _i64], _i32),
+    "sbfa_decode_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f64, _i32,
+                             _i64, _i64, _vp, _i64, _i64, _vp], _i32),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -168,6 +168,32 @@ int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
  * run sbfa_fwd with n_q == 1, as upstream does). */
 int sbfa_decode_supported(int dtype, int64_t head_dim);
 
+/* sbfa_decode without any device allocation by anyone.  No counterpart in
+ * the upstream project, which has no decode entry point at all.
+ *
+ * For callers that cannot allocate device memory around a decode step: a
+ * serving loop that reserved all of its memory up front, or runs the step
+ * under a fixed budget, and so may not call cudaMalloc (or grow a caching
+ * allocator) per token; a host embedding libsbfa through a plain C FFI with
+ * no device allocator of its own.  They pass only Q, K, V, the outputs and
+ * the block mask (same meaning as sbfa_decode); the decode plan and the
+ * split-KV partials live in an 8 MiB array inside the library, present on
+ * every GPU that loads it until the process exits.
+ *  - Shapes whose plan plus partials exceed 8 MiB are rejected with
+ *    SBFA_ERR_INVALID before any launch; use sbfa_decode for those.
+ *  - The first call on each device resolves that device's copy of the
+ *    array (cudaGetSymbolAddress); make that first call before capturing
+ *    the stream into a graph.
+ *  - All calls on a device share the one array and it keeps the last call's
+ *    contents (each call rewrites what it reads first); calls that can run
+ *    at the same time on the GPU (different streams, or graphs replayed
+ *    concurrently) race on it and must be serialised by the caller. */
+int sbfa_decode_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                        int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
+                        double softmax_scale, int is_causal, int64_t sink, int64_t window,
+                        const int32_t* block_mask, int64_t block_m, int64_t block_n,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif
