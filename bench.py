@@ -81,19 +81,12 @@ class Dist:
             self.pg.barrier()
 
     def max(self, x: float) -> float:
-        if not self.pg:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
-        return float(t.item())
+        import shard
+        return shard.max_over_ranks(x)
 
     def gather_checksums(self, vals):
-        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
-        if not self.pg:
-            return [t.tolist()]
-        out = [torch.empty_like(t) for _ in range(self.world)]
-        self.pg.all_gather(out, t)
-        return [o.tolist() for o in out]
+        import shard
+        return shard.gather_values(vals)
 
     def close(self):
         if self.pg:
