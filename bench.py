@@ -215,7 +215,7 @@ def time_steps(dist, step, steps: int, warmup: int):
     return dist.max(ms), launches, per_kernel
 
 
-def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None):
+def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None, workload=""):
     if not per_kernel:
         return None
     name, (tot, cnt) = max(per_kernel.items(), key=lambda kv: kv[1][0])
@@ -235,7 +235,7 @@ def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None):
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as fh:
-            traffic = json.load(fh).get(name)
+            traffic = json.load(fh).get(f"{name}@{workload}")
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
             "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_source": f"{peak_src} ({'sustained' if sustained and bound == 'tensor' else 'burst'})",
@@ -317,7 +317,7 @@ def bench_fwdbwd(dist, args, pk, src):
         "value": round(3.5 * F * dist.world * e_steps / (e_ms / 1e3) / 1e12, 3),
         "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d, "d2h_bytes_per_step": bytes_d2h,
         "ms_per_step": round(e_ms / e_steps, 3)}
-    rl = roofline(per_kernel, F, pk, src, sustained=True)
+    rl = roofline(per_kernel, F, pk, src, sustained=True, workload="cfg2")
     res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
                nnz=nnz, flops_fwd=F, finite=finite, per_kernel=per_kernel)
     del q, k, v, do, hq, hk, hv, hdo, out_h
@@ -340,7 +340,7 @@ def bench_fwd(dist, args, pk, src):
 
     ms, launches, per_kernel = time_steps(dist, step, max(2, args.steps), args.warmup)
     value = F * dist.world * max(2, args.steps) / (ms / 1e3) / 1e12
-    rl = roofline(per_kernel, F, pk, src, sustained=False)
+    rl = roofline(per_kernel, F, pk, src, sustained=False, workload="cfg3")
     del q, k, v
     torch.cuda.empty_cache()
     return dict(value=value, ms=ms / max(2, args.steps), roofline=rl, nnz=nnz, launches=launches)
@@ -362,7 +362,7 @@ def bench_decode(dist, args, pk, src):
     steps = max(5, args.steps * 5)
     ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
     value = kv_bytes * dist.world * steps / (ms / 1e3) / 1e9
-    rl = roofline(per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes)
+    rl = roofline(per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes, workload="cfg4")
     del q, k, v
     torch.cuda.empty_cache()
     return dict(value=value, ms=ms / steps, roofline=rl, kv_bytes=kv_bytes, qo_bytes=qo_bytes,
