@@ -5,25 +5,24 @@
 // Both kernels share one structure.  A CTA owns one 128-row tile of the
 // "resident" operand (keys for dK/dV, queries for dQ) and walks the kept
 // tiles of the other operand from the compacted plan (CSC for dK/dV, CSR
-// for dQ).  Every visited 128-wide tile is processed as two 64-wide
-// half-steps u = 2*i + h so that the score tiles S and dP can be double
-// buffered in TMEM:
-//   warp 0       TMA producer (resident tiles once, then a ring of streamed
-//                tile pairs; the dK/dV producer also stages LSE*log2(e) and
-//                Delta of each streamed query tile in shared memory);
-//   warp 1       MMA issuer: S[u%2] and dP[u%2] for half-step u, then, once
-//                the compute group published dS (and P) for u, the
-//                accumulator MMAs, then S/dP for u+2 into the same slot;
-//   warps 4-11   two compute groups that both work on every half-step:
-//                one TMEM lane (row) per thread, group g takes score columns
-//                [32g, 32g+32) of the half-step, computes
-//                P = 2^(S*scale*log2e - LSE*log2e) on visible pairs and
-//                dS = P * (dP - Delta) * scale, packs them to 16 bits and
-//                writes them over the first 16 of the 32 TMEM columns it just
-//                read (so the groups never touch each other's inputs); the
-//                accumulator MMAs read them there as the A operand.
-// TMEM (512 columns): S[0] 0-63, S[1] 64-127, dP[0] 128-191, dP[1] 192-255,
-// accumulators from 256 (dV, dK for the dK/dV kernel; dQ for the dQ kernel).
+// for dQ):
+//   warp 0       TMA producer (resident tiles once, then the streamed tiles;
+//                the dK/dV producer also stages LSE*log2(e) and Delta of
+//                each streamed query tile in shared memory);
+//   warp 1       MMA issuer: score tiles S and dP for step u, then, once the
+//                compute groups published dS (and P) for u, the accumulator
+//                MMAs, then the scores of a later step into the freed slot;
+//   warps 4-11   two compute groups that both work on every step: one TMEM
+//                lane (row) per thread, each group a contiguous half of the
+//                score columns; P = 2^(S*scale*log2e - LSE*log2e) on visible
+//                pairs and dS = P * (dP - Delta) * scale, packed to 16 bits
+//                over the first half of the TMEM columns just read (the
+//                groups never touch each other's inputs); the accumulator
+//                MMAs read them there as the A operand.
+// The dK/dV kernel splits every 128-wide streamed tile into two 64-wide
+// half-steps (S and dP double buffered, 64 TMEM columns each, accumulators
+// dV, dK from column 256).  The dQ kernel scores whole 128-key tiles; its
+// layout is described above the kernel.
 // Epilogue: accumulators -> 16-bit -> shared memory (128-byte swizzle) -> TMA
 // store; rows past the sequence end are clipped by the tensor map.
 #include <cuda.h>
@@ -47,8 +46,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTS = 0, kTDP = 128, kTAcc = 256;
 
-// TMEM column (within a 64-column slot) of the packed 16-bit A operand for
-// k-step kk of an accumulator MMA: compute group g stores its 32 score
+// TMEM column (within a 64-column slot of the dK/dV kernel) of the packed
+// 16-bit A operand for k-step kk of an accumulator MMA: compute group g stores its 32 score
 // columns, packed, at slot columns [32g, 32g+16).
 __device__ __forceinline__ uint32_t a_col(int kk) {
   return 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
@@ -363,27 +362,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------------------------
 // dQ
 // ---------------------------------------------------------------------------
-template <int D, int KST>
+// The dQ kernel scores whole 128-key tiles (N=128 MMAs run at the tensor
+// pipe's full rate, N=64 ones do not).  TMEM: S[0] 0-127, S[1] 128-255,
+// dP 256-383, dQ 384-.  Streamed tiles share one ring of kRing entries,
+// entry 2j = V_j and 2j+1 = K_j: V_j is only read by dP(j) and is released
+// early, so the ring refills with the next tiles while dQ_j still reads K_j.
+// MMA order: S(0) dP(0) S(1) | dP(j+1), dQ_j, S(j+2) for j = 0, 1, ...
+// Compute group g takes keys [64g, 64g+64) of every tile and writes its
+// packed dS over S columns [64g, 64g+32) of the same slot.
+constexpr int kRing = 5;
+
+// TMEM column (within a 128-column S slot) of the packed 16-bit dS for
+// k-step kk (16 keys) of the dQ MMA.
+__device__ __forceinline__ uint32_t a_col128(int kk) {
+  return 64u * (uint32_t)(kk >> 2) + 8u * (uint32_t)(kk & 3);
+}
+
+template <int D>
 struct DqLayout {
   static constexpr uint32_t kTile = kT * D * 2;
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t DO = Q + kTile;
-  static constexpr uint32_t K0 = DO + kTile;          // KST key tiles
-  static constexpr uint32_t V0 = K0 + KST * kTile;    // KST value tiles
-  static constexpr uint32_t BAR = V0 + KST * kTile;
+  static constexpr uint32_t RING = DO + kTile;       // kRing streamed tiles
+  static constexpr uint32_t BAR = RING + kRing * kTile;
   static constexpr int kQFull = 0;
-  static constexpr int kKFull = 1;                 // [KST]
-  static constexpr int kKEmpty = 1 + KST;          // [KST]
-  static constexpr int kSFull = 1 + 2 * KST;       // [2]
-  static constexpr int kPFull = 3 + 2 * KST;       // [2]
-  static constexpr int kDone = 5 + 2 * KST;
-  static constexpr int kDrain = 6 + 2 * KST;
-  static constexpr int kNumBars = 7 + 2 * KST;
+  static constexpr int kRFull = 1;                   // [kRing]
+  static constexpr int kREmpty = 1 + kRing;          // [kRing]
+  static constexpr int kSDFull = 1 + 2 * kRing;      // [2] S(j) and dP(j) written
+  static constexpr int kDPFree = 3 + 2 * kRing;      // compute read dP(j)
+  static constexpr int kPReady = 4 + 2 * kRing;      // compute wrote dS(j)
+  static constexpr int kDone = 5 + 2 * kRing;
+  static constexpr int kDrain = 6 + 2 * kRing;
+  static constexpr int kNumBars = 7 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kAlloc = MISC + 16 + 1024;
 };
 
-template <typename T, int D, int KST>
+template <typename T, int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -391,11 +406,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  const float* __restrict__ lse, const float* __restrict__ delta, float scale,
                  float scale_log2, MaskParams mp, const int32_t* __restrict__ row_ptr,
                  const int32_t* __restrict__ col_idx, int* status) {
-  using L = DqLayout<D, KST>;
+  using L = DqLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kH, false, false);   // M=128 q, N=64 keys
+  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 q, N=128 keys
   constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 q, N=D
   constexpr int kBoxes = D / 64;
+  constexpr uint32_t kTS0 = 0, kTDP = 256, kTDQ = 384;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -410,7 +426,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int bh = blockIdx.y;
   const int e0 = row_ptr[ti];
   const int nk = row_ptr[ti + 1] - e0;
-  const int U = 2 * nk;
 
   if (nk == 0) {  // the tile's rows see no key: dQ = 0
     for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
@@ -425,14 +440,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::kQFull), 1);
-    for (int s = 0; s < KST; ++s) {
-      mbar_init(bar(L::kKFull + s), 1);
-      mbar_init(bar(L::kKEmpty + s), 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(L::kRFull + s), 1);
+      mbar_init(bar(L::kREmpty + s), 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(bar(L::kSFull + x), 1);
-      mbar_init(bar(L::kPFull + x), 256);
-    }
+    mbar_init(bar(L::kSDFull), 1);
+    mbar_init(bar(L::kSDFull + 1), 1);
+    mbar_init(bar(L::kDPFree), 256);
+    mbar_init(bar(L::kPReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
@@ -458,73 +473,96 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       int issued = 0;
       int next_ent = col_idx[e0];
-      for (int j = 0; j < nk; ++j) {
-        const int s = j % KST, f = j / KST;
+      bool ok = true;
+      for (int j = 0; ok && j < nk; ++j) {
         const int kt = plan_index(next_ent);
         if (j + 1 < nk) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
-        if (f > 0 && !wait_bar(bar(L::kKEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status))
-          break;
-        mbar_expect_tx(bar(L::kKFull + s), 2 * L::kTile);
-        for (int r = 0; r < kBoxes; ++r) {
-          tma_load_3d(sb + L::K0 + s * L::kTile + r * 16384u, &tmk, bar(L::kKFull + s), 64 * r,
-                      kt * kT, bh);
-          tma_load_3d(sb + L::V0 + s * L::kTile + r * 16384u, &tmv, bar(L::kKFull + s), 64 * r,
-                      kt * kT, bh);
+        for (int part = 0; part < 2; ++part) {           // V_j, then K_j
+          const int e = 2 * j + part, s = e % kRing, f = e / kRing;
+          if (f > 0 &&
+              !wait_bar(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(bar(L::kRFull + s), L::kTile);
+          for (int r = 0; r < kBoxes; ++r)
+            tma_load_3d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmk : &tmv,
+                        bar(L::kRFull + s), 64 * r, kt * kT, bh);
+          issued = e + 1;
         }
-        issued = j + 1;
       }
       wait_bar_drain(bar(L::kQFull), 0, status);
-      for (int s = 0; s < KST; ++s) {
-        const int fills = issued > s ? (issued - 1 - s) / KST + 1 : 0;
-        if (fills) wait_bar_drain(bar(L::kKFull + s), (uint32_t)((fills - 1) & 1), status);
+      for (int s = 0; s < kRing; ++s) {
+        const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
+        if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
       }
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       // base descriptors, built once; MMAs add constant offsets
       const uint64_t d_q = desc_kmajor(sb + L::Q), d_g = desc_kmajor(sb + L::DO);
-      const uint64_t d_k0 = desc_kmajor(sb + L::K0), d_v0 = desc_kmajor(sb + L::V0);
-      const uint64_t m_k0 = desc_mnmajor(sb + L::K0, 16384u);
-      auto issue_sdp = [&](int u) -> bool {
-        const int j = u >> 1, h = u & 1, s = j % KST, slot = u & 1;
-        if (h == 0 &&
-            !wait_bar(bar(L::kKFull + s), (uint32_t)((j / KST) & 1), abort_flag, status))
+      const uint64_t d_r = desc_kmajor(sb + L::RING);
+      const uint64_t m_r = desc_mnmajor(sb + L::RING, 16384u);
+      auto ring = [&](int e) -> bool {
+        if (!wait_bar(bar(L::kRFull + e % kRing), (uint32_t)((e / kRing) & 1), abort_flag,
+                      status))
           return false;
         tc_fence_after();
-        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
-        const uint64_t dk = desc_advance(d_k0, half), dv = desc_advance(d_v0, half);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTS + 64u * slot, desc_advance(d_q, off), desc_advance(dk, off),
-                     kIdescS, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTDP + 64u * slot, desc_advance(d_g, off), desc_advance(dv, off),
-                     kIdescS, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(L::kSFull + slot));
         return true;
       };
-      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status);
-      if (ok) ok = issue_sdp(0);
-      if (ok && U > 1) ok = issue_sdp(1);
-      for (int u = 0; ok && u < U; ++u) {
-        const int j = u >> 1, h = u & 1, s = j % KST, slot = u & 1;
-        if (!wait_bar(bar(L::kPFull + slot), (uint32_t)(j & 1), abort_flag, status)) {
+      // scores: tdst[128 x 128] = A (resident, K-major) * ring entry e^T
+      auto scores = [&](uint32_t tdst, uint64_t da, int e) {
+        const uint64_t db = desc_advance(d_r, (uint32_t)(e % kRing) * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss(tmem + tdst, desc_advance(da, off), desc_advance(db, off), kIdescS,
+                     kk > 0 ? 1u : 0u);
+        }
+      };
+      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status) && ring(1);
+      if (ok) {
+        scores(kTS0, d_q, 1);  // S(0) = Q K_0^T
+        ok = ring(0);
+      }
+      if (ok) {
+        scores(kTDP, d_g, 0);  // dP(0) = dO V_0^T
+        tc_commit(bar(L::kSDFull));
+        tc_commit(bar(L::kREmpty + 0));
+        if (nk > 1) {
+          ok = ring(3);
+          if (ok) scores(kTS0 + 128u, d_q, 3);  // S(1)
+        }
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        if (j + 1 < nk) {  // dP(j+1) once the compute groups have read dP(j)
+          if (!wait_bar(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status) ||
+              !ring(2 * j + 2)) {
+            ok = false;
+            break;
+          }
+          scores(kTDP, d_g, 2 * j + 2);
+          tc_commit(bar(L::kSDFull + ((j + 1) & 1)));
+          tc_commit(bar(L::kREmpty + (2 * j + 2) % kRing));
+        }
+        if (!wait_bar(bar(L::kPReady), (uint32_t)(j & 1), abort_flag, status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t mk = desc_advance(m_k0, s * L::kTile + (uint32_t)h * 8192u);
+        const uint64_t mk = desc_advance(m_r, (uint32_t)((2 * j + 1) % kRing) * L::kTile);
+        const uint32_t ts = tmem + kTS0 + 128u * (uint32_t)(j & 1);
 #pragma unroll
-        for (int kk = 0; kk < kH / 16; ++kk)  // dQ += dS K
-          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
-                     desc_advance(mk, (uint32_t)kk * 2048u), kIdescAcc,
-                     (u > 0 || kk > 0) ? 1u : 0u);
-        if (h == 1) tc_commit(bar(L::kKEmpty + s));
-        if (u + 2 < U) ok = issue_sdp(u + 2);
+        for (int kk = 0; kk < kT / 16; ++kk)  // dQ += dS_j K_j
+          mma_f16_ts(tmem + kTDQ, ts + a_col128(kk), desc_advance(mk, (uint32_t)kk * 2048u),
+                     kIdescAcc, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(bar(L::kREmpty + (2 * j + 1) % kRing));
+        if (j + 2 < nk) {  // S(j+2) into the slot dQ_j just read (MMAs run in order)
+          if (!ring(2 * j + 5)) {
+            ok = false;
+            break;
+          }
+          scores(kTS0 + 128u * (uint32_t)(j & 1), d_q, 2 * j + 5);
+        }
       }
       tc_commit(bar(L::kDone));
       tc_commit(bar(L::kDrain));
@@ -533,7 +571,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     regs_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 4) >> 2;  // column half of every half-step this group takes
+    const int grp = (warp - 4) >> 2;  // key half of every tile this group takes
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int row = ti * kT + r;
@@ -542,45 +580,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
     const float dl = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
     bool ok = true;
-    for (int u = 0; u < U; ++u) {
-      const int j = u >> 1, h = u & 1, slot = u & 1;
+    for (int j = 0; j < nk; ++j) {
       const int32_t ent = col_idx[e0 + j];
-      uint32_t vis[1];
-      row_visibility<32>(vis, mp, row, plan_index(ent) * kT + kH * h + 32 * grp,
-                         plan_partial(ent));
-      ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kSFull + slot), (uint32_t)(j & 1), abort_flag, status));
+      uint32_t vis[2];
+      row_visibility<64>(vis, mp, row, plan_index(ent) * kT + 64 * grp, plan_partial(ent));
+      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kSDFull + (j & 1)), (uint32_t)((j >> 1) & 1),
+                                            abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t t_s = tmem + lane_base + kTS + 64u * slot + 32u * grp;
-      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * slot + 32u * grp;
-      uint32_t sv[32], dpv[32];
+      const uint32_t t_s = tmem + lane_base + kTS0 + 128u * (uint32_t)(j & 1) + 64u * grp;
+      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
+      uint32_t sv[64], dpv[64];
       tmem_ld32(t_s, sv);
+      tmem_ld32(t_s + 32u, sv + 32);
       tmem_ld32(t_dp, dpv);
+      tmem_ld32(t_dp + 32u, dpv + 32);
       tmem_wait_ld();
-      uint32_t ds2[16];
+      tc_fence_before();
+      mbar_arrive(bar(L::kDPFree));
+      uint32_t ds2[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 32; ++c) {
         float d[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int cc = 2 * c + e;
-          const bool on = (vis[0] >> cc) & 1u;
+          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
           const float p = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lse2) : 0.f;
           d[e] = p * (__uint_as_float(dpv[cc]) - dl) * scale;
         }
         ds2[c] = pack2<T>(d[0], d[1]);
       }
-      tmem_st16(t_s, ds2);
+      tmem_st32(t_s, ds2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull + slot));
+      mbar_arrive(bar(L::kPReady));
     }
     // epilogue: dQ columns [64*grp, 64*grp + 64) staged in Q's buffer
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
     if (ok && 64 * grp < D) {
       tc_fence_after();
-      const uint32_t t_acc = tmem + lane_base + kTAcc + 64u * grp;
+      const uint32_t t_acc = tmem + lane_base + kTDQ + 64u * grp;
       const uint32_t region = sb + L::Q + (uint32_t)grp * 16384u;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -617,7 +657,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-template <typename T, int D, int QST, int KST>
+template <typename T, int D, int QST>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
                   const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
@@ -647,8 +687,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
   }
   if (int rc = check_launch("dkdv_tc_kernel")) return rc;
   {
-    using L = DqLayout<D, KST>;
-    auto kern = dq_tc_kernel<T, D, KST>;
+    using L = DqLayout<D>;
+    auto kern = dq_tc_kernel<T, D>;
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)L::kAlloc),
                             "cudaFuncSetAttribute(dq_tc)"))
@@ -673,16 +713,16 @@ int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const 
   if (int rc = generic_delta(dtype, o, dout, delta, (int64_t)BH * mp.n_q, D, s)) return rc;
   const bool bf = dtype == SBFA_BF16;
   if (D == 128)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 128, 2, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+    return bf ? launch_bwd_tc<__nv_bfloat16, 128, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
                                                         scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
                                                         status, s)
-              : launch_bwd_tc<__half, 128, 2, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+              : launch_bwd_tc<__half, 128, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
                                                  mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   if (D == 64)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 64, 4, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+    return bf ? launch_bwd_tc<__nv_bfloat16, 64, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
                                                        scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
                                                        status, s)
-              : launch_bwd_tc<__half, 64, 4, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+              : launch_bwd_tc<__half, 64, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
                                                 mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward: head_dim must be 64 or 128");
 }
