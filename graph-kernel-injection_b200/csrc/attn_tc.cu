@@ -171,12 +171,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int fills = issued > s ? (issued - 1 - s) / STAGES + 1 : 0;
         if (fills) wait_bar_drain(bar(L::kKVFull + s), (uint32_t)((fills - 1) & 1), status);
       }
-   } else if (warp == 1 && lane == 0) {
+   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     {
       auto kv_wait = [&](int e) -> bool {
-        return wait_bar(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
-                        status);
+        return wait_bar_w(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
+                          status);
       };
       // base descriptors, built once; MMAs add constant offsets
       const uint64_t dq0 = desc_kmajor(sb + L::Q);
@@ -188,61 +188,61 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + 128u * x, desc_advance(dq, off), desc_advance(dk, off), kIdescQK,
-                     kk > 0 ? 1u : 0u);
+          mma_f16_ss_w(tmem + 128u * x, desc_advance(dq, off), desc_advance(dk, off), kIdescQK,
+                       kk > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int x, int e, bool acc) {
         const uint64_t dv = desc_advance(dkv_v, (uint32_t)(e % STAGES) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < kTN / 16; ++kk)
-          mma_f16_ts(tmem + 256u + 128u * x, tmem + 128u * x + 64u + 8u * kk,
-                     desc_advance(dv, (uint32_t)kk * 2048u), kIdescPV, (acc || kk > 0) ? 1u : 0u);
+          mma_f16_ts_w(tmem + 256u + 128u * x, tmem + 128u * x + 64u + 8u * kk,
+                       desc_advance(dv, (uint32_t)kk * 2048u), kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
-      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status) && kv_wait(0);
+      bool ok = wait_bar_w(bar(L::kQFull), 0, abort_flag, status) && kv_wait(0);
       if (ok) {
         tc_fence_after();
         qk(0, 0);
-        tc_commit(bar(L::kSFull + 0));
+        tc_commit_w(bar(L::kSFull + 0));
         qk(1, 0);
-        tc_commit(bar(L::kSFull + 1));
-        tc_commit(bar(L::kKVEmpty + 0));
+        tc_commit_w(bar(L::kSFull + 1));
+        tc_commit_w(bar(L::kKVEmpty + 0));
       }
       for (int j = 1; ok && j < n; ++j) {
         const int ev = 2 * j - 1, ek = 2 * j;
         const uint32_t ph = (uint32_t)((j - 1) & 1);
         if (!(kv_wait(ev) && kv_wait(ek))) { ok = false; break; }
-        if (!wait_bar(bar(L::kPFull + 0), ph, abort_flag, status)) { ok = false; break; }
+        if (!wait_bar_w(bar(L::kPFull + 0), ph, abort_flag, status)) { ok = false; break; }
         tc_fence_after();
         pv(0, ev, j > 1);
         qk(0, ek);
-        tc_commit(bar(L::kSFull + 0));
-        if (!wait_bar(bar(L::kPFull + 1), ph, abort_flag, status)) { ok = false; break; }
+        tc_commit_w(bar(L::kSFull + 0));
+        if (!wait_bar_w(bar(L::kPFull + 1), ph, abort_flag, status)) { ok = false; break; }
         tc_fence_after();
         pv(1, ev, j > 1);
-        tc_commit(bar(L::kKVEmpty + ev % STAGES));
+        tc_commit_w(bar(L::kKVEmpty + ev % STAGES));
         qk(1, ek);
-        tc_commit(bar(L::kSFull + 1));
-        tc_commit(bar(L::kKVEmpty + ek % STAGES));
+        tc_commit_w(bar(L::kSFull + 1));
+        tc_commit_w(bar(L::kKVEmpty + ek % STAGES));
       }
       if (ok) {
         const int ev = 2 * n - 1;
         const uint32_t ph = (uint32_t)((n - 1) & 1);
-        ok = kv_wait(ev) && wait_bar(bar(L::kPFull + 0), ph, abort_flag, status);
+        ok = kv_wait(ev) && wait_bar_w(bar(L::kPFull + 0), ph, abort_flag, status);
         if (ok) {
           tc_fence_after();
           pv(0, ev, n > 1);
-          tc_commit(bar(L::kOFull + 0));
-          ok = wait_bar(bar(L::kPFull + 1), ph, abort_flag, status);
+          tc_commit_w(bar(L::kOFull + 0));
+          ok = wait_bar_w(bar(L::kPFull + 1), ph, abort_flag, status);
         }
         if (ok) {
           tc_fence_after();
           pv(1, ev, n > 1);
-          tc_commit(bar(L::kOFull + 1));
-          tc_commit(bar(L::kKVEmpty + ev % STAGES));
+          tc_commit_w(bar(L::kOFull + 1));
+          tc_commit_w(bar(L::kKVEmpty + ev % STAGES));
         }
       }
-      tc_commit(bar(L::kDrain));
+      tc_commit_w(bar(L::kDrain));
       wait_bar_drain(bar(L::kDrain), 0, status);
     }
    }

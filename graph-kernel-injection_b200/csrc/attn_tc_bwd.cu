@@ -4,25 +4,22 @@
 //
 // Both kernels share one structure.  A CTA owns one 128-row tile of the
 // "resident" operand (keys for dK/dV, queries for dQ) and walks the kept
-// tiles of the other operand from the compacted plan (CSC for dK/dV, CSR
-// for dQ):
-//   warp 0       TMA producer (resident tiles once, then the streamed tiles;
-//                the dK/dV producer also stages LSE*log2(e) and Delta of
-//                each streamed query tile in shared memory);
-//   warp 1       MMA issuer: score tiles S and dP for step u, then, once the
-//                compute groups published dS (and P) for u, the accumulator
-//                MMAs, then the scores of a later step into the freed slot;
-//   warps 4-11   two compute groups that both work on every step: one TMEM
-//                lane (row) per thread, each group a contiguous half of the
-//                score columns; P = 2^(S*scale*log2e - LSE*log2e) on visible
-//                pairs and dS = P * (dP - Delta) * scale, packed to 16 bits
-//                over the first half of the TMEM columns just read (the
-//                groups never touch each other's inputs); the accumulator
-//                MMAs read them there as the A operand.
-// The dK/dV kernel splits every 128-wide streamed tile into two 64-wide
-// half-steps (S and dP double buffered, 64 TMEM columns each, accumulators
-// dV, dK from column 256).  The dQ kernel scores whole 128-key tiles; its
-// layout is described above the kernel.
+// 128-row tiles of the other operand from the compacted plan (CSC for
+// dK/dV, CSR for dQ), scoring whole 128 x 128 tiles (N = 128 MMAs run at the
+// tensor pipe's full rate, N = 64 ones do not):
+//   warp 0       TMA producer: the resident tiles once, then the streamed
+//                tiles through a ring of kRing shared-memory entries (the
+//                dK/dV producer also stages LSE*log2(e) and Delta of each
+//                streamed query tile in shared memory);
+//   warp 1       MMA issuer, the whole warp with one elected lane issuing
+//                (warp-uniform descriptors stay in uniform registers);
+//   warps 4-11   two compute groups that both work on every tile: one TMEM
+//                lane (row) per thread, group g takes score columns
+//                [64g, 64g+64); P = 2^(S*scale*log2e - LSE*log2e) on visible
+//                pairs and dS = P * (dP - Delta), packed to 16 bits over TMEM
+//                columns the group has already read, where the accumulator
+//                MMAs read them as the A operand.
+// The TMEM layout and MMA order of each kernel are described above it.
 // Epilogue: accumulators -> 16-bit -> shared memory (128-byte swizzle) -> TMA
 // store; rows past the sequence end are clipped by the tensor map.
 #include <cuda.h>
@@ -38,48 +35,70 @@ namespace {
 using namespace tc;
 
 constexpr int kT = 128;        // rows of a resident / streamed tile
-constexpr int kH = 64;         // width of a half-step
+constexpr int kRing = 5;       // streamed tiles in flight (shared-memory ring entries)
 constexpr int kBwdThreads = 384;
 constexpr int kRegsCtl = 64;
 constexpr int kRegsCompute = 208;  // 128*64 + 256*208 <= 384*168
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTS = 0, kTDP = 128, kTAcc = 256;
 
-// TMEM column (within a 64-column slot of the dK/dV kernel) of the packed
-// 16-bit A operand for k-step kk of an accumulator MMA: compute group g stores its 32 score
-// columns, packed, at slot columns [32g, 32g+16).
-__device__ __forceinline__ uint32_t a_col(int kk) {
-  return 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
+// TMEM column, within a 128-column score buffer, of the packed 16-bit A
+// operand for k-step kk (16 score columns) of an accumulator MMA: compute
+// group g packs score columns [64g, 64g+64) into buffer columns
+// [64g, 64g+32).
+__device__ __forceinline__ uint32_t a_col128(int kk) {
+  return 64u * (uint32_t)(kk >> 2) + 8u * (uint32_t)(kk & 3);
 }
 
 // ---------------------------------------------------------------------------
 // dK / dV
 // ---------------------------------------------------------------------------
-template <int D, int QST>
+// A CTA owns 128 keys and walks the query tiles that see them (CSC plan).
+// TMEM: two 128-column score buffers that swap roles every tile -- tile i
+// computes S_i^T = K Q_i^T into buf[i&1] and dP_i^T = V dO_i^T into
+// buf[(i+1)&1] -- then dV at 256 and dK at 384.  Compute group g (query
+// columns [64g, 64g+64) of the tile) writes P packed to 16 bits over
+// buf[i&1] columns [64g, 64g+32) and dS over [64g+32, 64g+64), i.e. over the
+// S values it has already read; so once the groups have read dP_i its
+// buffer takes S_{i+1} at once, and dP_{i+1} follows dK_i into buf[i&1]
+// (MMAs from one issuer run in order).  MMA order per tile:
+//   [P_i ready] dV += P_i^T dO_i, [dP_i read] S_{i+1},
+//   [dS_i ready] dK += dS_i^T Q_i, dP_{i+1}.
+// Streamed tiles share one ring of kRing entries, entry 2i = Q_i and
+// 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
+// dK once in the epilogue.
+template <int D>
 struct DkdvLayout {
   static constexpr uint32_t kTile = kT * D * 2;
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + kTile;
-  static constexpr uint32_t Q0 = V + kTile;                // QST query tiles
-  static constexpr uint32_t DO0 = Q0 + QST * kTile;        // QST dO tiles
-  static constexpr uint32_t LS = DO0 + QST * kTile;        // QST x 128 floats (LSE * log2 e)
-  static constexpr uint32_t DL = LS + QST * kT * 4;        // QST x 128 floats (Delta)
-  static constexpr uint32_t BAR = DL + QST * kT * 4;
+  static constexpr uint32_t RING = V + kTile;               // kRing streamed tiles
+  static constexpr uint32_t LS = RING + kRing * kTile;      // 2 x 128 floats (LSE * log2 e)
+  static constexpr uint32_t DL = LS + 2 * kT * 4;           // 2 x 128 floats (Delta)
+  static constexpr uint32_t BAR = DL + 2 * kT * 4;
   static constexpr int kKVFull = 0;
-  static constexpr int kQFull = 1;                 // [QST]
-  static constexpr int kQEmpty = 1 + QST;          // [QST]
-  static constexpr int kSFull = 1 + 2 * QST;       // [2]
-  static constexpr int kPFull = 3 + 2 * QST;       // [2]
-  static constexpr int kDone = 5 + 2 * QST;
-  static constexpr int kDrain = 6 + 2 * QST;
-  static constexpr int kLFull = 7 + 2 * QST;       // [QST] LSE/Delta staged
-  static constexpr int kNumBars = 7 + 3 * QST;
+  static constexpr int kRFull = 1;                   // [kRing]
+  static constexpr int kREmpty = 1 + kRing;          // [kRing]
+  static constexpr int kLFull = 1 + 2 * kRing;       // [2] LSE / Delta slot staged
+  static constexpr int kLEmpty = 3 + 2 * kRing;      // [2] slot read by the compute groups
+  static constexpr int kSFull = 5 + 2 * kRing;       // S_i written
+  static constexpr int kDPFull = 6 + 2 * kRing;      // dP_i written
+  static constexpr int kPReady = 7 + 2 * kRing;      // P_i packed in TMEM
+  static constexpr int kDPRead = 8 + 2 * kRing;      // dP_i read into registers
+  static constexpr int kDSReady = 9 + 2 * kRing;     // dS_i packed in TMEM
+  static constexpr int kDone = 10 + 2 * kRing;
+  static constexpr int kDrain = 11 + 2 * kRing;
+  static constexpr int kNumBars = 12 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
-  static constexpr uint32_t kAlloc = MISC + 16 + 1024;
+  static constexpr uint32_t kBytes = MISC + 16;
+  // D = 128 leaves no room to align the window by hand: the kernel checks
+  // that the runtime placed it on a 1024-byte boundary (it does when the
+  // kernel has no static shared memory) and reports otherwise.
+  static constexpr bool kAlignInKernel = kBytes + 1024 <= 232448;
+  static constexpr uint32_t kAlloc = kAlignInKernel ? kBytes + 1024 : kBytes;
 };
 
-template <typename T, int D, int QST>
+template <typename T, int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -88,28 +107,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                    T* __restrict__ dv, const float* __restrict__ lse,
                    const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
                    const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
-                   int* status) {
-  using L = DkdvLayout<D, QST>;
+                   int n_tj, int* status) {
+  using L = DkdvLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kH, false, false);   // M=128 keys, N=64 q
+  constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
   constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 keys, N=D
   constexpr int kBoxes = D / 64;
+  constexpr uint32_t kTDV = 256, kTDK = 384;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = smem_raw;
+  if (L::kAlignInKernel) {
+    smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  } else if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) record_status(status, kStatusBadSmemAlign);
+    return;
+  }
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) -> uint32_t { return sb + L::BAR + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // sink-heavy key tiles come first: all heads of key tile 0, then tile 1, ...
-  const int tj = blockIdx.x / BH;
-  const int bh = blockIdx.x % BH;
+  // the sink key tiles (seen by every query tile) first, one per (b, h);
+  // then each (b, h)'s remaining key tiles in order, so CTAs running side by
+  // side stream the same query tiles through L2
+  int tj, bh;
+  if ((int)blockIdx.x < BH) {
+    tj = 0;
+    bh = blockIdx.x;
+  } else {
+    const int idx = blockIdx.x - BH;
+    bh = idx / (n_tj - 1);
+    tj = 1 + idx % (n_tj - 1);
+  }
   const int e0 = col_ptr[tj];
   const int nq = col_ptr[tj + 1] - e0;
-  const int U = 2 * nq;
 
   if (nq == 0) {  // no query sees this key tile: dK = dV = 0
     for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
@@ -126,15 +160,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::kKVFull), 1);
-    for (int s = 0; s < QST; ++s) {
-      mbar_init(bar(L::kQFull + s), 1);
-      mbar_init(bar(L::kQEmpty + s), 1);
-      mbar_init(bar(L::kLFull + s), 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(L::kRFull + s), 1);
+      mbar_init(bar(L::kREmpty + s), 1);
     }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(bar(L::kSFull + x), 1);
-      mbar_init(bar(L::kPFull + x), 256);
+      mbar_init(bar(L::kLFull + x), 1);
+      mbar_init(bar(L::kLEmpty + x), 256);
     }
+    mbar_init(bar(L::kSFull), 1);
+    mbar_init(bar(L::kDPFull), 1);
+    mbar_init(bar(L::kPReady), 256);
+    mbar_init(bar(L::kDPRead), 256);
+    mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
@@ -162,30 +200,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       int issued = 0;
       int next_ent = row_idx[e0];
-      for (int i = 0; i < nq; ++i) {
-        const int s = i % QST, f = i / QST;
+      bool ok = true;
+      for (int i = 0; ok && i < nq; ++i) {
         const int ti = plan_index(next_ent);
         if (i + 1 < nq) next_ent = row_idx[e0 + i + 1];  // prefetch the next plan entry
-        if (f > 0) {
-          const bool ok = __all_sync(0xffffffffu, wait_bar(bar(L::kQEmpty + s),
-                                                           (uint32_t)((f - 1) & 1), abort_flag,
-                                                           status));
-          if (!ok) break;
-        }
-        // tensor copies first: the MMA warp only needs Q and dO
-        if (lane == 0) {
-          mbar_expect_tx(bar(L::kQFull + s), 2 * L::kTile);
-          for (int r = 0; r < kBoxes; ++r) {
-            tma_load_3d(sb + L::Q0 + s * L::kTile + r * 16384u, &tmq, bar(L::kQFull + s), 64 * r,
-                        ti * kT, bh);
-            tma_load_3d(sb + L::DO0 + s * L::kTile + r * 16384u, &tmdo, bar(L::kQFull + s),
-                        64 * r, ti * kT, bh);
+        for (int part = 0; part < 2; ++part) {           // Q_i, then dO_i
+          const int e = 2 * i + part, s = e % kRing, f = e / kRing;
+          if (f > 0 && !wait_bar_w(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag,
+                                   status)) {
+            ok = false;
+            break;
           }
+          if (lane == 0) {
+            mbar_expect_tx(bar(L::kRFull + s), L::kTile);
+            for (int r = 0; r < kBoxes; ++r)
+              tma_load_3d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmdo : &tmq,
+                          bar(L::kRFull + s), 64 * r, ti * kT, bh);
+          }
+          issued = e + 1;
         }
-        issued = i + 1;
-        // then the per-row LSE (log2 units) and Delta for the compute groups
-        float* ls = reinterpret_cast<float*>(smem + L::LS) + s * kT;
-        float* dl = reinterpret_cast<float*>(smem + L::DL) + s * kT;
+        if (!ok) break;
+        // then the per-row LSE (log2 units) and Delta of the tile
+        const int slot = i & 1;
+        if (i >= 2 && !wait_bar_w(bar(L::kLEmpty + slot), (uint32_t)(((i >> 1) - 1) & 1),
+                                  abort_flag, status))
+          break;
+        float* ls = reinterpret_cast<float*>(smem + L::LS) + slot * kT;
+        float* dl = reinterpret_cast<float*>(smem + L::DL) + slot * kT;
         for (int rr = lane; rr < kT; rr += 32) {
           const int row = ti * kT + rr;
           const bool in = row < mp.n_q;
@@ -193,132 +234,186 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           dl[rr] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::kLFull + s));
+        if (lane == 0) mbar_arrive(bar(L::kLFull + slot));
       }
       if (lane == 0) {
         wait_bar_drain(bar(L::kKVFull), 0, status);
-        for (int s = 0; s < QST; ++s) {
-          const int fills = issued > s ? (issued - 1 - s) / QST + 1 : 0;
-          if (fills) wait_bar_drain(bar(L::kQFull + s), (uint32_t)((fills - 1) & 1), status);
+        for (int s = 0; s < kRing; ++s) {
+          const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
+          if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
         }
       }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
-      // base descriptors, built once; MMAs add constant offsets
       const uint64_t d_k = desc_kmajor(sb + L::K), d_v = desc_kmajor(sb + L::V);
-      const uint64_t d_q0 = desc_kmajor(sb + L::Q0), d_g0 = desc_kmajor(sb + L::DO0);
-      const uint64_t m_q0 = desc_mnmajor(sb + L::Q0, 16384u);
-      const uint64_t m_g0 = desc_mnmajor(sb + L::DO0, 16384u);
-      auto issue_sdp = [&](int u) -> bool {
-        const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
-        if (h == 0 &&
-            !wait_bar(bar(L::kQFull + s), (uint32_t)((i / QST) & 1), abort_flag, status))
+      const uint64_t d_r = desc_kmajor(sb + L::RING);
+      const uint64_t m_r = desc_mnmajor(sb + L::RING, 16384u);
+      auto ring = [&](int e) -> bool {
+        if (!wait_bar_w(bar(L::kRFull + e % kRing), (uint32_t)((e / kRing) & 1), abort_flag,
+                        status))
           return false;
         tc_fence_after();
-        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
-        const uint64_t dq = desc_advance(d_q0, half), dg = desc_advance(d_g0, half);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTS + 64u * slot, desc_advance(d_k, off), desc_advance(dq, off),
-                     kIdescS, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + kTDP + 64u * slot, desc_advance(d_v, off), desc_advance(dg, off),
-                     kIdescS, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(L::kSFull + slot));
         return true;
       };
-      bool ok = wait_bar(bar(L::kKVFull), 0, abort_flag, status);
-      if (ok) ok = issue_sdp(0);
-      if (ok && U > 1) ok = issue_sdp(1);
-      for (int u = 0; ok && u < U; ++u) {
-        const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
-        if (!wait_bar(bar(L::kPFull + slot), (uint32_t)(i & 1), abort_flag, status)) {
-          ok = false;
-          break;
+      // tdst[128 keys x 128 q] = A (K or V, K-major) * (ring entry e)^T
+      auto scores = [&](uint32_t tdst, uint64_t da, int e) {
+        const uint64_t db = desc_advance(d_r, (uint32_t)(e % kRing) * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          mma_f16_ss_w(tmem + tdst, desc_advance(da, off), desc_advance(db, off), kIdescS,
+                       kk > 0 ? 1u : 0u);
         }
-        tc_fence_after();
-        const uint32_t half = s * L::kTile + (uint32_t)h * 8192u;
-        const uint64_t mg = desc_advance(m_g0, half), mq = desc_advance(m_q0, half);
+      };
+      // tacc[128 keys x D] += packed A (TMEM columns tsrc + a_col128) * ring entry e
+      auto accum = [&](uint32_t tacc, uint32_t tsrc, int e, bool acc) {
+        const uint64_t mb = desc_advance(m_r, (uint32_t)(e % kRing) * L::kTile);
 #pragma unroll
-        for (int kk = 0; kk < kH / 16; ++kk)  // dV += P^T dO
-          mma_f16_ts(tmem + kTAcc, tmem + kTS + 64u * slot + a_col(kk),
-                     desc_advance(mg, (uint32_t)kk * 2048u), kIdescAcc,
-                     (u > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < kH / 16; ++kk)  // dK += dS^T Q
-          mma_f16_ts(tmem + kTAcc + 128u, tmem + kTDP + 64u * slot + a_col(kk),
-                     desc_advance(mq, (uint32_t)kk * 2048u), kIdescAcc,
-                     (u > 0 || kk > 0) ? 1u : 0u);
-        if (h == 1) tc_commit(bar(L::kQEmpty + s));
-        if (u + 2 < U) ok = issue_sdp(u + 2);
+        for (int kk = 0; kk < kT / 16; ++kk)
+          mma_f16_ts_w(tmem + tacc, tmem + tsrc + a_col128(kk),
+                       desc_advance(mb, (uint32_t)kk * 2048u), kIdescAcc,
+                       (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = wait_bar_w(bar(L::kKVFull), 0, abort_flag, status) && ring(0);
+      if (ok) {
+        scores(0u, d_k, 0);  // S_0 -> buf[0]
+        tc_commit_w(bar(L::kSFull));
+        ok = ring(1);
       }
-      tc_commit(bar(L::kDone));
-      tc_commit(bar(L::kDrain));
+      if (ok) {
+        scores(128u, d_v, 1);  // dP_0 -> buf[1]
+        tc_commit_w(bar(L::kDPFull));
+      }
+      for (int i = 0; ok && i < nq; ++i) {
+        const uint32_t buf = 128u * (uint32_t)(i & 1), other = 128u - buf;
+        const uint32_t ph = (uint32_t)(i & 1);
+        if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
+        tc_fence_after();
+        accum(kTDV, buf, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
+        tc_commit_w(bar(L::kREmpty + (2 * i + 1) % kRing));
+        if (i + 1 < nq) {
+          if (!wait_bar_w(bar(L::kDPRead), ph, abort_flag, status) || !ring(2 * i + 2)) break;
+          scores(other, d_k, 2 * i + 2);  // S_{i+1} -> the buffer dP_i has left
+          tc_commit_w(bar(L::kSFull));
+        }
+        if (!wait_bar_w(bar(L::kDSReady), ph, abort_flag, status)) break;
+        tc_fence_after();
+        accum(kTDK, buf + 32u, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
+        tc_commit_w(bar(L::kREmpty + (2 * i) % kRing));
+        if (i + 1 < nq) {
+          if (!ring(2 * i + 3)) break;
+          scores(buf, d_v, 2 * i + 3);  // dP_{i+1} -> buf[i&1], after dV_i / dK_i read it
+          tc_commit_w(bar(L::kDPFull));
+        }
+      }
+      tc_commit_w(bar(L::kDone));
+      tc_commit_w(bar(L::kDrain));
       wait_bar_drain(bar(L::kDrain), 0, status);
     }
   } else {
     regs_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 4) >> 2;  // column half of every half-step this group takes
+    const int grp = (warp - 4) >> 2;  // query columns [64*grp, 64*grp + 64) of every tile
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int key = tj * kT + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
-    for (int u = 0; u < U; ++u) {
-      const int i = u >> 1, h = u & 1, s = i % QST, slot = u & 1;
+    for (int i = 0; i < nq; ++i) {
+      const int slot = i & 1;
+      const uint32_t ph = (uint32_t)(i & 1);
       const int32_t ent = row_idx[e0 + i];
-      const int c0 = kH * h + 32 * grp;  // first of this group's 32 query columns in the tile
-      uint32_t vis[1];
-      col_visibility<32>(vis, mp, key, plan_index(ent) * kT + c0, plan_partial(ent));
+      const int q0 = plan_index(ent) * kT + 64 * grp;
+      uint32_t vis[2];
+      col_visibility<64>(vis, mp, key, q0, plan_partial(ent));
+      const bool all_vis = __all_sync(0xffffffffu, (vis[0] & vis[1]) == 0xffffffffu);
       ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kLFull + s), (uint32_t)((i / QST) & 1), abort_flag, status) &&
-                          wait_bar(bar(L::kSFull + slot), (uint32_t)(i & 1), abort_flag, status));
+                      wait_bar(bar(L::kLFull + slot), (uint32_t)((i >> 1) & 1), abort_flag,
+                               status) &&
+                          wait_bar(bar(L::kSFull), ph, abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t t_s = tmem + lane_base + kTS + 64u * slot + 32u * grp;
-      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * slot + 32u * grp;
-      uint32_t sv[32], dpv[32];
-      tmem_ld32(t_s, sv);
-      tmem_ld32(t_dp, dpv);
-      tmem_wait_ld();
-      const float4* ls4 = reinterpret_cast<const float4*>(smem + L::LS) + (s * kT + c0) / 4;
-      const float4* dl4 = reinterpret_cast<const float4*>(smem + L::DL) + (s * kT + c0) / 4;
-      uint32_t pk[16], dk2[16];
+      const uint32_t t_s = tmem + lane_base + 128u * (uint32_t)(i & 1) + 64u * grp;
+      const uint32_t t_dp = tmem + lane_base + 128u * (uint32_t)((i + 1) & 1) + 64u * grp;
+      const float4* ls4 = reinterpret_cast<const float4*>(smem + L::LS) + (slot * kT + 64 * grp) / 4;
+      const float4* dl4 = reinterpret_cast<const float4*>(smem + L::DL) + (slot * kT + 64 * grp) / 4;
+      // P = 2^(S * scale * log2 e - LSE * log2 e) on visible pairs
+      float p[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(t_s, sv);
+        tmem_ld32(t_s + 32u, sv + 32);
+        tmem_wait_ld();
+        if (all_vis) {
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        const float4 l4 = ls4[q4], d4 = dl4[q4];
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-        float p[4], d[4];
+          for (int q4 = 0; q4 < 16; ++q4) {
+            const float4 l4 = ls4[q4];
+            p[4 * q4 + 0] = ex2(fmaf(__uint_as_float(sv[4 * q4 + 0]), scale_log2, -l4.x));
+            p[4 * q4 + 1] = ex2(fmaf(__uint_as_float(sv[4 * q4 + 1]), scale_log2, -l4.y));
+            p[4 * q4 + 2] = ex2(fmaf(__uint_as_float(sv[4 * q4 + 2]), scale_log2, -l4.z));
+            p[4 * q4 + 3] = ex2(fmaf(__uint_as_float(sv[4 * q4 + 3]), scale_log2, -l4.w));
+          }
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int cc = 4 * q4 + e;
-          const bool on = (vis[0] >> cc) & 1u;
-          p[e] = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lv[e]) : 0.f;
-          d[e] = p[e] * (__uint_as_float(dpv[cc]) - dv4[e]) * scale;
+          for (int q4 = 0; q4 < 16; ++q4) {
+            const float4 l4 = ls4[q4];
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int cc = 4 * q4 + e;
+              const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
+              p[cc] = on ? ex2(fmaf(__uint_as_float(sv[cc]), scale_log2, -lv[e])) : 0.f;
+            }
+          }
         }
-        pk[2 * q4] = pack2<T>(p[0], p[1]);
-        pk[2 * q4 + 1] = pack2<T>(p[2], p[3]);
-        dk2[2 * q4] = pack2<T>(d[0], d[1]);
-        dk2[2 * q4 + 1] = pack2<T>(d[2], d[3]);
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = pack2<T>(p[2 * c], p[2 * c + 1]);
+        tmem_st32(t_s, pk);
       }
-      tmem_st16(t_s, pk);
-      tmem_st16(t_dp, dk2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull + slot));
+      mbar_arrive(bar(L::kPReady));
+      // dS = P * (dP - Delta), in two 32-column halves
+      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDPFull), ph, abort_flag, status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t dsk[32];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t dpv[32];
+        tmem_ld32(t_dp + 32u * hf, dpv);
+        tmem_wait_ld();
+        if (hf == 1) {
+          tc_fence_before();
+          mbar_arrive(bar(L::kDPRead));
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 d4 = dl4[8 * hf + q4];
+          const int c = 32 * hf + 4 * q4;
+          const float a0 = p[c + 0] * (__uint_as_float(dpv[4 * q4 + 0]) - d4.x);
+          const float a1 = p[c + 1] * (__uint_as_float(dpv[4 * q4 + 1]) - d4.y);
+          const float a2 = p[c + 2] * (__uint_as_float(dpv[4 * q4 + 2]) - d4.z);
+          const float a3 = p[c + 3] * (__uint_as_float(dpv[4 * q4 + 3]) - d4.w);
+          dsk[16 * hf + 2 * q4] = pack2<T>(a0, a1);
+          dsk[16 * hf + 2 * q4 + 1] = pack2<T>(a2, a3);
+        }
+      }
+      mbar_arrive(bar(L::kLEmpty + slot));  // the LSE / Delta slot has been read
+      tmem_st32(t_s + 32u, dsk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(L::kDSReady));
     }
-    // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes dK
-    // (staged in V's buffer); both buffers are free once every MMA is done
+    // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes
+    // dK * scale (staged in V's buffer); both buffers are free once every
+    // MMA is done
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
     if (ok) {
       tc_fence_after();
-      const uint32_t t_acc = tmem + lane_base + kTAcc + 128u * grp;
+      const uint32_t t_acc = tmem + lane_base + (grp == 0 ? kTDV : kTDK);
+      const float mul = grp == 0 ? 1.f : scale;
       const uint32_t stage = sb + (grp == 0 ? L::K : L::V);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -328,7 +423,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int i2 = 0; i2 < 16; ++i2)
-          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]), __uint_as_float(t[2 * i2 + 1]));
+          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]) * mul, __uint_as_float(t[2 * i2 + 1]) * mul);
         const uint32_t region = stage + (uint32_t)((32 * c) >> 6) * 16384u;
 #pragma unroll
         for (int i2 = 0; i2 < 4; ++i2) {
@@ -362,22 +457,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------------------------
 // dQ
 // ---------------------------------------------------------------------------
-// The dQ kernel scores whole 128-key tiles (N=128 MMAs run at the tensor
-// pipe's full rate, N=64 ones do not).  TMEM: S[0] 0-127, S[1] 128-255,
-// dP 256-383, dQ 384-.  Streamed tiles share one ring of kRing entries,
-// entry 2j = V_j and 2j+1 = K_j: V_j is only read by dP(j) and is released
-// early, so the ring refills with the next tiles while dQ_j still reads K_j.
+// A CTA owns 128 queries and walks the key tiles they see (CSR plan).
+// TMEM: S[0] 0-127, S[1] 128-255, dP 256-383, dQ 384-.  Streamed tiles
+// share one ring of kRing entries, entry 2j = V_j and 2j+1 = K_j: V_j is
+// only read by dP(j) and is released early, so the ring refills with the
+// next tiles while dQ_j still reads K_j.
 // MMA order: S(0) dP(0) S(1) | dP(j+1), dQ_j, S(j+2) for j = 0, 1, ...
 // Compute group g takes keys [64g, 64g+64) of every tile and writes its
 // packed dS over S columns [64g, 64g+32) of the same slot.
-constexpr int kRing = 5;
-
-// TMEM column (within a 128-column S slot) of the packed 16-bit dS for
-// k-step kk (16 keys) of the dQ MMA.
-__device__ __forceinline__ uint32_t a_col128(int kk) {
-  return 64u * (uint32_t)(kk >> 2) + 8u * (uint32_t)(kk & 3);
-}
-
 template <int D>
 struct DqLayout {
   static constexpr uint32_t kTile = kT * D * 2;
@@ -496,15 +583,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
         if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
       }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
       // base descriptors, built once; MMAs add constant offsets
       const uint64_t d_q = desc_kmajor(sb + L::Q), d_g = desc_kmajor(sb + L::DO);
       const uint64_t d_r = desc_kmajor(sb + L::RING);
       const uint64_t m_r = desc_mnmajor(sb + L::RING, 16384u);
       auto ring = [&](int e) -> bool {
-        if (!wait_bar(bar(L::kRFull + e % kRing), (uint32_t)((e / kRing) & 1), abort_flag,
-                      status))
+        if (!wait_bar_w(bar(L::kRFull + e % kRing), (uint32_t)((e / kRing) & 1), abort_flag,
+                        status))
           return false;
         tc_fence_after();
         return true;
@@ -515,19 +602,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss(tmem + tdst, desc_advance(da, off), desc_advance(db, off), kIdescS,
-                     kk > 0 ? 1u : 0u);
+          mma_f16_ss_w(tmem + tdst, desc_advance(da, off), desc_advance(db, off), kIdescS,
+                       kk > 0 ? 1u : 0u);
         }
       };
-      bool ok = wait_bar(bar(L::kQFull), 0, abort_flag, status) && ring(1);
+      bool ok = wait_bar_w(bar(L::kQFull), 0, abort_flag, status) && ring(1);
       if (ok) {
         scores(kTS0, d_q, 1);  // S(0) = Q K_0^T
         ok = ring(0);
       }
       if (ok) {
         scores(kTDP, d_g, 0);  // dP(0) = dO V_0^T
-        tc_commit(bar(L::kSDFull));
-        tc_commit(bar(L::kREmpty + 0));
+        tc_commit_w(bar(L::kSDFull));
+        tc_commit_w(bar(L::kREmpty + 0));
         if (nk > 1) {
           ok = ring(3);
           if (ok) scores(kTS0 + 128u, d_q, 3);  // S(1)
@@ -535,16 +622,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk) {  // dP(j+1) once the compute groups have read dP(j)
-          if (!wait_bar(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status) ||
+          if (!wait_bar_w(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status) ||
               !ring(2 * j + 2)) {
             ok = false;
             break;
           }
           scores(kTDP, d_g, 2 * j + 2);
-          tc_commit(bar(L::kSDFull + ((j + 1) & 1)));
-          tc_commit(bar(L::kREmpty + (2 * j + 2) % kRing));
+          tc_commit_w(bar(L::kSDFull + ((j + 1) & 1)));
+          tc_commit_w(bar(L::kREmpty + (2 * j + 2) % kRing));
         }
-        if (!wait_bar(bar(L::kPReady), (uint32_t)(j & 1), abort_flag, status)) {
+        if (!wait_bar_w(bar(L::kPReady), (uint32_t)(j & 1), abort_flag, status)) {
           ok = false;
           break;
         }
@@ -553,9 +640,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t ts = tmem + kTS0 + 128u * (uint32_t)(j & 1);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)  // dQ += dS_j K_j
-          mma_f16_ts(tmem + kTDQ, ts + a_col128(kk), desc_advance(mk, (uint32_t)kk * 2048u),
-                     kIdescAcc, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(bar(L::kREmpty + (2 * j + 1) % kRing));
+          mma_f16_ts_w(tmem + kTDQ, ts + a_col128(kk), desc_advance(mk, (uint32_t)kk * 2048u),
+                       kIdescAcc, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit_w(bar(L::kREmpty + (2 * j + 1) % kRing));
         if (j + 2 < nk) {  // S(j+2) into the slot dQ_j just read (MMAs run in order)
           if (!ring(2 * j + 5)) {
             ok = false;
@@ -564,8 +651,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           scores(kTS0 + 128u * (uint32_t)(j & 1), d_q, 2 * j + 5);
         }
       }
-      tc_commit(bar(L::kDone));
-      tc_commit(bar(L::kDrain));
+      tc_commit_w(bar(L::kDone));
+      tc_commit_w(bar(L::kDrain));
       wait_bar_drain(bar(L::kDrain), 0, status);
     }
   } else {
@@ -657,7 +744,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-template <typename T, int D, int QST>
+template <typename T, int D>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
                   const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
@@ -674,8 +761,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
   if (int rc = make_tmap_3d(&mdv, dv, kBF16, D, nkv, bh, kT)) return rc;
   const float sl = scale * kLog2e;
   {
-    using L = DkdvLayout<D, QST>;
-    auto kern = dkdv_tc_kernel<T, D, QST>;
+    using L = DkdvLayout<D>;
+    auto kern = dkdv_tc_kernel<T, D>;
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)L::kAlloc),
                             "cudaFuncSetAttribute(dkdv_tc)"))
@@ -683,7 +770,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     const int n_tj = ceil_div_i(mp.n_kv, kT);
     LaunchScope ls("dkdv_tc_kernel", s);
     kern<<<n_tj * BH, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse,
-                                                  delta, scale, sl, mp, kv_cp, kv_ri, BH, status);
+                                                  delta, scale, sl, mp, kv_cp, kv_ri, BH, n_tj,
+                                                  status);
   }
   if (int rc = check_launch("dkdv_tc_kernel")) return rc;
   {
@@ -713,16 +801,16 @@ int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const 
   if (int rc = generic_delta(dtype, o, dout, delta, (int64_t)BH * mp.n_q, D, s)) return rc;
   const bool bf = dtype == SBFA_BF16;
   if (D == 128)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 128, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+    return bf ? launch_bwd_tc<__nv_bfloat16, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
                                                         scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
                                                         status, s)
-              : launch_bwd_tc<__half, 128, 2>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+              : launch_bwd_tc<__half, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
                                                  mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   if (D == 64)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 64, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
+    return bf ? launch_bwd_tc<__nv_bfloat16, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
                                                        scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
                                                        status, s)
-              : launch_bwd_tc<__half, 64, 4>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+              : launch_bwd_tc<__half, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
                                                 mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward: head_dim must be 64 or 128");
 }

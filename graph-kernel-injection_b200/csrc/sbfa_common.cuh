@@ -103,6 +103,7 @@ int* device_status_ptr();
 
 // Status codes a kernel may record (first writer wins).
 constexpr int kStatusWaitTimeout = 1;
+constexpr int kStatusBadSmemAlign = 2;
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

@@ -53,7 +53,8 @@ int sbfa_last_error(char* buf, size_t len);
 /* Read and clear the device status word of the current device (a blocking
  * device->host read of 4 bytes).  0 = no kernel reported a failure since
  * the last call; otherwise the first failure code a kernel recorded
- * (1 = a bounded wait on a pipeline barrier expired). */
+ * (1 = a bounded wait on a pipeline barrier expired, 2 = a kernel found its
+ * dynamic shared memory window not 1024-byte aligned and wrote nothing). */
 int sbfa_device_status(int* status_out);
 
 /* Total kernel launches issued by this library in this process. */
