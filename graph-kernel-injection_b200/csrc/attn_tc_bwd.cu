@@ -8,9 +8,9 @@
 // dK/dV, CSR for dQ), scoring whole 128 x 128 tiles (N = 128 MMAs run at the
 // tensor pipe's full rate, N = 64 ones do not):
 //   warp 0       TMA producer: the resident tiles once, then the streamed
-//                tiles through a ring of kRing shared-memory entries (the
-//                dK/dV producer also stages LSE*log2(e) and Delta of each
-//                streamed query tile in shared memory);
+//                tiles through a ring of kRing shared-memory entries;
+//   warp 2       (dK/dV only) stages LSE*log2(e) and Delta of each streamed
+//                query tile in shared memory;
 //   warp 1       MMA issuer, the whole warp with one elected lane issuing
 //                (warp-uniform descriptors stay in uniform registers);
 //   warps 4-11   two compute groups that both work on every tile: one TMEM
@@ -54,16 +54,15 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
 // dK / dV
 // ---------------------------------------------------------------------------
 // A CTA owns 128 keys and walks the query tiles that see them (CSC plan).
-// TMEM: two 128-column score buffers that swap roles every tile -- tile i
-// computes S_i^T = K Q_i^T into buf[i&1] and dP_i^T = V dO_i^T into
-// buf[(i+1)&1] -- then dV at 256 and dK at 384.  Compute group g (query
-// columns [64g, 64g+64) of the tile) writes P packed to 16 bits over
-// buf[i&1] columns [64g, 64g+32) and dS over [64g+32, 64g+64), i.e. over the
-// S values it has already read; so once the groups have read dP_i its
-// buffer takes S_{i+1} at once, and dP_{i+1} follows dK_i into buf[i&1]
-// (MMAs from one issuer run in order).  MMA order per tile:
-//   [P_i ready] dV += P_i^T dO_i, [dP_i read] S_{i+1},
+// TMEM: S_i^T = K Q_i^T at 0-127, dP_i^T = V dO_i^T at 128-255, dV at 256,
+// dK at 384.  Compute group g (query columns [64g, 64g+64) of the tile)
+// writes P_i packed to 16 bits over S columns [64g, 64g+32) and dS_i over
+// dP columns [64g, 64g+32), i.e. over values it has already read.  MMAs
+// from one issuer run in order, so S_{i+1} follows dV_i (the reader of P_i)
+// and dP_{i+1} follows dK_i (the reader of dS_i) without further waits:
+//   [P_i ready] dV += P_i^T dO_i, S_{i+1},
 //   [dS_i ready] dK += dS_i^T Q_i, dP_{i+1}.
+// The MMAs for S_{i+1} run while the compute groups work on dS_i.
 // Streamed tiles share one ring of kRing entries, entry 2i = Q_i and
 // 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
 // dK once in the epilogue.
@@ -84,11 +83,10 @@ struct DkdvLayout {
   static constexpr int kSFull = 5 + 2 * kRing;       // S_i written
   static constexpr int kDPFull = 6 + 2 * kRing;      // dP_i written
   static constexpr int kPReady = 7 + 2 * kRing;      // P_i packed in TMEM
-  static constexpr int kDPRead = 8 + 2 * kRing;      // dP_i read into registers
-  static constexpr int kDSReady = 9 + 2 * kRing;     // dS_i packed in TMEM
-  static constexpr int kDone = 10 + 2 * kRing;
-  static constexpr int kDrain = 11 + 2 * kRing;
-  static constexpr int kNumBars = 12 + 2 * kRing;
+  static constexpr int kDSReady = 8 + 2 * kRing;     // dS_i packed in TMEM
+  static constexpr int kDone = 9 + 2 * kRing;
+  static constexpr int kDrain = 10 + 2 * kRing;
+  static constexpr int kNumBars = 11 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kBytes = MISC + 16;
   // D = 128 leaves no room to align the window by hand: the kernel checks
@@ -113,7 +111,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
   constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 keys, N=D
   constexpr int kBoxes = D / 64;
-  constexpr uint32_t kTDV = 256, kTDK = 384;
+  constexpr uint32_t kTS = 0, kTDP = 128, kTDV = 256, kTDK = 384;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
@@ -171,7 +169,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kSFull), 1);
     mbar_init(bar(L::kDPFull), 1);
     mbar_init(bar(L::kPReady), 256);
-    mbar_init(bar(L::kDPRead), 256);
     mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
@@ -219,22 +216,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           issued = e + 1;
         }
-        if (!ok) break;
-        // then the per-row LSE (log2 units) and Delta of the tile
-        const int slot = i & 1;
-        if (i >= 2 && !wait_bar_w(bar(L::kLEmpty + slot), (uint32_t)(((i >> 1) - 1) & 1),
-                                  abort_flag, status))
-          break;
-        float* ls = reinterpret_cast<float*>(smem + L::LS) + slot * kT;
-        float* dl = reinterpret_cast<float*>(smem + L::DL) + slot * kT;
-        for (int rr = lane; rr < kT; rr += 32) {
-          const int row = ti * kT + rr;
-          const bool in = row < mp.n_q;
-          ls[rr] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
-          dl[rr] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::kLFull + slot));
       }
       if (lane == 0) {
         wait_bar_drain(bar(L::kKVFull), 0, status);
@@ -242,6 +223,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
           if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
         }
+      }
+    } else if (warp == 2) {
+      // ------------------------------------------- LSE (log2 units) / Delta
+      // a warp of its own, so the latency of these loads never delays the
+      // tensor copies
+      for (int i = 0; i < nq; ++i) {
+        const int slot = i & 1;
+        const int ti = plan_index(row_idx[e0 + i]);
+        const int row0 = ti * kT;
+        float lv[kT / 32], dv2[kT / 32];
+#pragma unroll
+        for (int c = 0; c < kT / 32; ++c) {  // loads first, then the wait for the slot
+          const int row = row0 + 32 * c + lane;
+          const bool in = row < mp.n_q;
+          lv[c] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
+          dv2[c] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
+        }
+        if (i >= 2 && !wait_bar_w(bar(L::kLEmpty + slot), (uint32_t)(((i >> 1) - 1) & 1),
+                                  abort_flag, status))
+          break;
+        float* ls = reinterpret_cast<float*>(smem + L::LS) + slot * kT;
+        float* dl = reinterpret_cast<float*>(smem + L::DL) + slot * kT;
+#pragma unroll
+        for (int c = 0; c < kT / 32; ++c) {
+          ls[32 * c + lane] = lv[c];
+          dl[32 * c + lane] = dv2[c];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::kLFull + slot));
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
@@ -276,33 +286,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       };
       bool ok = wait_bar_w(bar(L::kKVFull), 0, abort_flag, status) && ring(0);
       if (ok) {
-        scores(0u, d_k, 0);  // S_0 -> buf[0]
+        scores(kTS, d_k, 0);  // S_0
         tc_commit_w(bar(L::kSFull));
         ok = ring(1);
       }
       if (ok) {
-        scores(128u, d_v, 1);  // dP_0 -> buf[1]
+        scores(kTDP, d_v, 1);  // dP_0
         tc_commit_w(bar(L::kDPFull));
       }
       for (int i = 0; ok && i < nq; ++i) {
-        const uint32_t buf = 128u * (uint32_t)(i & 1), other = 128u - buf;
         const uint32_t ph = (uint32_t)(i & 1);
         if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
         tc_fence_after();
-        accum(kTDV, buf, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
+        accum(kTDV, kTS, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
         tc_commit_w(bar(L::kREmpty + (2 * i + 1) % kRing));
         if (i + 1 < nq) {
-          if (!wait_bar_w(bar(L::kDPRead), ph, abort_flag, status) || !ring(2 * i + 2)) break;
-          scores(other, d_k, 2 * i + 2);  // S_{i+1} -> the buffer dP_i has left
+          if (!ring(2 * i + 2)) break;
+          scores(kTS, d_k, 2 * i + 2);  // S_{i+1}, after dV_i has read P_i
           tc_commit_w(bar(L::kSFull));
         }
         if (!wait_bar_w(bar(L::kDSReady), ph, abort_flag, status)) break;
         tc_fence_after();
-        accum(kTDK, buf + 32u, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
+        accum(kTDK, kTDP, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
         tc_commit_w(bar(L::kREmpty + (2 * i) % kRing));
         if (i + 1 < nq) {
           if (!ring(2 * i + 3)) break;
-          scores(buf, d_v, 2 * i + 3);  // dP_{i+1} -> buf[i&1], after dV_i / dK_i read it
+          scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dK_i has read dS_i
           tc_commit_w(bar(L::kDPFull));
         }
       }
@@ -333,8 +342,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                           wait_bar(bar(L::kSFull), ph, abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t t_s = tmem + lane_base + 128u * (uint32_t)(i & 1) + 64u * grp;
-      const uint32_t t_dp = tmem + lane_base + 128u * (uint32_t)((i + 1) & 1) + 64u * grp;
+      const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
+      const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
       const float4* ls4 = reinterpret_cast<const float4*>(smem + L::LS) + (slot * kT + 64 * grp) / 4;
       const float4* dl4 = reinterpret_cast<const float4*>(smem + L::DL) + (slot * kT + 64 * grp) / 4;
       // P = 2^(S * scale * log2 e - LSE * log2 e) on visible pairs
@@ -384,10 +393,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t dpv[32];
         tmem_ld32(t_dp + 32u * hf, dpv);
         tmem_wait_ld();
-        if (hf == 1) {
-          tc_fence_before();
-          mbar_arrive(bar(L::kDPRead));
-        }
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4) {
           const float4 d4 = dl4[8 * hf + q4];
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       mbar_arrive(bar(L::kLEmpty + slot));  // the LSE / Delta slot has been read
-      tmem_st32(t_s + 32u, dsk);
+      tmem_st32(t_dp, dsk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(L::kDSReady));
