@@ -259,12 +259,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t t_o = tmem + lane_base + 256u + 128u * x;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    int32_t ent_next = col_idx[e0];
     for (int j = 0; j < n; ++j) {
-      const int32_t ent = col_idx[e0 + j];
+      const int32_t ent = ent_next;
+      if (j + 1 < n) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
       const int k0 = plan_index(ent) * kTN;
       const bool partial = plan_partial(ent);
-      uint32_t vis[4];
-      row_visibility<kTN>(vis, mp, row, k0, partial);
+      uint32_t vis[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      const bool all_vis = block_all_visible(mp, row0 + x * kTM, kTM, k0, kTN, partial);
+      if (!all_vis) row_visibility<kTN>(vis, mp, row, k0, partial);
       ok = __all_sync(0xffffffffu,
                       wait_bar(bar(L::kSFull + x), (uint32_t)(j & 1), abort_flag, status));
       if (!ok) break;
@@ -273,24 +276,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
       for (int c = 0; c < kTN / 32; ++c) tmem_ld32(t_s + 32u * c, sv + 32 * c);
       tmem_wait_ld();
+      // row maximum of the raw scores; scale * log2(e) > 0 is applied after
       float rmax = -INFINITY;
-      if ((vis[0] & vis[1] & vis[2] & vis[3]) == 0xffffffffu) {
+      if (all_vis) {
 #pragma unroll
-        for (int c = 0; c < kTN; ++c) {
-          const float v = __uint_as_float(sv[c]) * scale_log2;
-          sv[c] = __float_as_uint(v);
-          rmax = fmaxf(rmax, v);
-        }
+        for (int c = 0; c < kTN; ++c) rmax = fmaxf(rmax, __uint_as_float(sv[c]));
       } else {
 #pragma unroll
         for (int c = 0; c < kTN; ++c) {
-          const float v = ((vis[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(sv[c]) * scale_log2
-                                                           : -INFINITY;
+          const float v = ((vis[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(sv[c]) : -INFINITY;
           sv[c] = __float_as_uint(v);
           rmax = fmaxf(rmax, v);
         }
       }
-      const float m_new = fmaxf(m_run, rmax);
+      const float m_new = fmaxf(m_run, rmax * scale_log2);
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
       if (__any_sync(0xffffffffu, need)) {
         // O_X already holds PV_X(j-1): it completed before S_X(j) did
@@ -317,8 +316,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = dead ? 0.f : ex2(__uint_as_float(sv[32 * c + 2 * i]) - m_run);
-          const float p1 = dead ? 0.f : ex2(__uint_as_float(sv[32 * c + 2 * i + 1]) - m_run);
+          const float p0 =
+              dead ? 0.f : ex2(fmaf(__uint_as_float(sv[32 * c + 2 * i]), scale_log2, -m_run));
+          const float p1 =
+              dead ? 0.f : ex2(fmaf(__uint_as_float(sv[32 * c + 2 * i + 1]), scale_log2, -m_run));
           rsum += p0 + p1;
           pk[i] = pack2<T>(p0, p1);
         }

@@ -328,14 +328,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int key = tj * kT + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
+    int32_t ent_next = row_idx[e0];
     for (int i = 0; i < nq; ++i) {
       const int slot = i & 1;
       const uint32_t ph = (uint32_t)(i & 1);
-      const int32_t ent = row_idx[e0 + i];
+      const int32_t ent = ent_next;
+      if (i + 1 < nq) ent_next = row_idx[e0 + i + 1];  // in flight while this tile runs
       const int q0 = plan_index(ent) * kT + 64 * grp;
-      uint32_t vis[2];
-      col_visibility<64>(vis, mp, key, q0, plan_partial(ent));
-      const bool all_vis = __all_sync(0xffffffffu, (vis[0] & vis[1]) == 0xffffffffu);
+      uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
+      const bool all_vis = block_all_visible(mp, q0, 64, tj * kT, kT, plan_partial(ent));
+      if (!all_vis) col_visibility<64>(vis, mp, key, q0, plan_partial(ent));
       ok = __all_sync(0xffffffffu,
                       wait_bar(bar(L::kLFull + slot), (uint32_t)((i >> 1) & 1), abort_flag,
                                status) &&
@@ -672,10 +674,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
     const float dl = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
     bool ok = true;
+    int32_t ent_next = col_idx[e0];
     for (int j = 0; j < nk; ++j) {
-      const int32_t ent = col_idx[e0 + j];
-      uint32_t vis[2];
-      row_visibility<64>(vis, mp, row, plan_index(ent) * kT + 64 * grp, plan_partial(ent));
+      const int32_t ent = ent_next;
+      if (j + 1 < nk) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
+      const int k0 = plan_index(ent) * kT + 64 * grp;
+      uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
+      const bool all_vis = block_all_visible(mp, ti * kT, kT, k0, 64, plan_partial(ent));
+      if (!all_vis) row_visibility<64>(vis, mp, row, k0, plan_partial(ent));
       ok = __all_sync(0xffffffffu, wait_bar(bar(L::kSDFull + (j & 1)), (uint32_t)((j >> 1) & 1),
                                             abort_flag, status));
       if (!ok) break;
@@ -690,18 +696,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar(L::kDPFree));
+      // dS = P * (dP - Delta); the softmax scale multiplies dQ in the epilogue
       uint32_t ds2[32];
+      if (all_vis) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        float d[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e;
-          const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
-          const float p = on ? ex2(__uint_as_float(sv[cc]) * scale_log2 - lse2) : 0.f;
-          d[e] = p * (__uint_as_float(dpv[cc]) - dl) * scale;
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = ex2(fmaf(__uint_as_float(sv[2 * c]), scale_log2, -lse2));
+          const float p1 = ex2(fmaf(__uint_as_float(sv[2 * c + 1]), scale_log2, -lse2));
+          ds2[c] = pack2<T>(p0 * (__uint_as_float(dpv[2 * c]) - dl),
+                            p1 * (__uint_as_float(dpv[2 * c + 1]) - dl));
         }
-        ds2[c] = pack2<T>(d[0], d[1]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          float d[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = 2 * c + e;
+            const bool on = (vis[cc >> 5] >> (cc & 31)) & 1u;
+            const float p = on ? ex2(fmaf(__uint_as_float(sv[cc]), scale_log2, -lse2)) : 0.f;
+            d[e] = p * (__uint_as_float(dpv[cc]) - dl);
+          }
+          ds2[c] = pack2<T>(d[0], d[1]);
+        }
       }
       tmem_st32(t_s, ds2);
       tmem_wait_st();
@@ -722,7 +739,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int i2 = 0; i2 < 16; ++i2)
-          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]), __uint_as_float(t[2 * i2 + 1]));
+          w[i2] = pack2<T>(__uint_as_float(t[2 * i2]) * scale, __uint_as_float(t[2 * i2 + 1]) * scale);
 #pragma unroll
         for (int i2 = 0; i2 < 4; ++i2) {
           const uint32_t addr = region + sw128_offset((uint32_t)r, 32u * c + 8u * i2);

@@ -21,6 +21,22 @@ __device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, in
   return true;
 }
 
+// True when every pair of query rows [q_lo, q_lo+nq) x keys [k_lo, k_lo+nk)
+// is visible (inside both sequences, lifted block mask all ones -- the plan
+// marks other tiles partial -- and, when causal, inside the token rule): a
+// few uniform integer tests that let the softmax phases skip the per-element
+// masks on interior tiles.
+__device__ __forceinline__ bool block_all_visible(const MaskParams& mp, int q_lo, int nq, int k_lo,
+                                                  int nk, bool partial) {
+  if (partial) return false;
+  const int q_hi = q_lo + nq - 1, k_hi = k_lo + nk - 1;
+  if (q_hi >= mp.n_q || k_hi >= mp.n_kv) return false;
+  if (!mp.causal) return true;
+  if (mp.q_off + q_lo < k_hi) return false;  // a key after a query
+  if (k_hi < mp.sink) return true;           // sink keys only
+  return mp.q_off + q_hi - max(k_lo, mp.sink) < mp.window;
+}
+
 // Visibility of the NCOL keys [k0, k0+NCOL) for one query row, bit c of
 // vis[c/32] = key k0 + c: sequence end, token rule when causal (at most two
 // intervals: sink and window), lifted block mask on partial tiles.
