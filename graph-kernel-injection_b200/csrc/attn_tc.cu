@@ -6,23 +6,24 @@
 //   warp 0      TMA producer: Q_A, Q_B once, then K_j, V_j of every kept key
 //               tile (plan CSR row, 256x128 tiles) into one STAGES-deep ring
 //               that alternates K and V tiles;
-//   warp 1      MMA issuer (one thread): S_X = Q_X K_j^T into TMEM, and
-//               O_X += P_X V_j with P_X read straight from TMEM;
-//   warps 2-3   idle;
+//   warps 1, 2  MMA issuers for tile A and tile B (whole warp, one elected
+//               lane issuing): S_X = Q_X K^T into TMEM, O_X += P_X V with
+//               P_X read straight from TMEM;
+//   warp 3      idle;
 //   warps 4-7   softmax for tile A, warps 8-11 for tile B: thread t of a group
-//               owns query row t (its TMEM lane), loads the row's 128 scores
-//               with tcgen05.ld, masks them with a 128-bit visibility mask
-//               built from intervals (token rule, sequence end) and the lifted
-//               block mask on partial tiles, runs the online softmax in base 2,
-//               rescales its O row in TMEM only when the running max grew by
-//               more than 2^8, and writes P (bf16/fp16) into the upper half of
-//               its S columns with tcgen05.st.
-// Schedule of the MMA thread per key tile j:
-//   PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j)
-// so softmax A(j) overlaps PV_B(j-1) + QK_B(j) and vice versa.  MMAs from one
-// thread execute in issue order, so QK_X(j) overwrites S_X/P_X only after
-// PV_X(j-1) has read P_X, and when S_X(j) is complete O_X already holds
-// PV_X(j-1) (no extra barrier for the O rescale).
+//               owns query row t (its TMEM lane).
+// Every key tile is processed as two 64-key half-steps u = 2j + h so that S_X
+// is double buffered: TMEM S_A [0,128) and S_B [128,256) each hold two 64-
+// column slots, O_A [256,384), O_B [384,512).  Per half-step the softmax
+// thread loads its 64 scores with tcgen05.ld, masks them (uniform all-visible
+// test, else a 64-bit mask from token-rule intervals, the sequence end and
+// the lifted block mask on partial tiles), runs the online softmax in base 2,
+// rescales its O row in TMEM only when the running max grew by more than
+// 2^8, and writes P (bf16/fp16) packed over the first 32 columns of the slot.
+// MMA warp X per half-step: [P_X(u) ready] PV_X(u), QK_X(u+2) into the same
+// slot.  MMAs from one thread execute in issue order, so QK_X(u+2) overwrites
+// the slot only after PV_X(u) has read P_X(u); the softmax of u+1 (other
+// slot) overlaps both.  An O rescale first waits for PV_X(u-1).
 // Epilogue: O rows are normalised, staged in the Q buffer (128-byte swizzle)
 // and written with a TMA store; LSE rows are stored directly.
 // Numerics as upstream: natural-log LSE = m + log(l), empty rows give
@@ -43,6 +44,7 @@ using namespace tc;
 constexpr int kTM = 128;   // rows per query tile (one TMEM lane per row)
 constexpr int kPair = 2;   // query tiles per CTA
 constexpr int kTN = 128;   // keys per key tile
+constexpr int kHalf = 64;  // keys per half-step (one 64-column S slot)
 constexpr int kFwdThreads = 384;
 constexpr int kRegsCtl = 64;       // producer / MMA warpgroup
 constexpr int kRegsSoftmax = 208;  // each softmax warpgroup (128*64 + 256*208 <= 384*168)
@@ -60,11 +62,14 @@ struct FwdLayout {
   static constexpr int kQFull = 0;
   static constexpr int kKVFull = 1;
   static constexpr int kKVEmpty = 1 + STAGES;
-  static constexpr int kSFull = 1 + 2 * STAGES;  // [2]
-  static constexpr int kPFull = 3 + 2 * STAGES;  // [2]
-  static constexpr int kOFull = 5 + 2 * STAGES;  // [2]
-  static constexpr int kDrain = 7 + 2 * STAGES;
-  static constexpr int kNumBars = 8 + 2 * STAGES;
+  // S and P barriers are per (tile x, slot h) at 2x + h: a softmax group
+  // may run one step ahead of the MMA warp, never two on the same slot
+  static constexpr int kSFull = 1 + 2 * STAGES;   // [4]
+  static constexpr int kPFull = 5 + 2 * STAGES;   // [4]
+  static constexpr int kPVDone = 9 + 2 * STAGES;  // [2]
+  static constexpr int kOFull = 11 + 2 * STAGES;  // [2]
+  static constexpr int kDrain = 13 + 2 * STAGES;  // [2]
+  static constexpr int kNumBars = 15 + 2 * STAGES;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;  // [0] TMEM base, [1] abort flag
   static constexpr uint32_t kBytes = MISC + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;     // room to align the base to 1 KB
@@ -79,7 +84,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   int* status) {
   using L = FwdLayout<D, STAGES>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescQK = idesc_f16(kBF16, kTM, kTN, false, false);
+  constexpr uint32_t kIdescQK = idesc_f16(kBF16, kTM, kHalf, false, false);
   constexpr uint32_t kIdescPV = idesc_f16(kBF16, kTM, D, false, true);
   constexpr int kBoxes = D / 64;  // 64-column boxes per tile row
 
@@ -116,14 +121,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(bar(L::kQFull), 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar(L::kKVFull + s), 1);
-      mbar_init(bar(L::kKVEmpty + s), 1);
+      mbar_init(bar(L::kKVEmpty + s), kPair);  // released by both MMA warps
     }
     for (int x = 0; x < kPair; ++x) {
-      mbar_init(bar(L::kSFull + x), 1);
-      mbar_init(bar(L::kPFull + x), 128);
+      mbar_init(bar(L::kSFull + 2 * x), 1);
+      mbar_init(bar(L::kSFull + 2 * x + 1), 1);
+      mbar_init(bar(L::kPFull + 2 * x), 128);
+      mbar_init(bar(L::kPFull + 2 * x + 1), 128);
+      mbar_init(bar(L::kPVDone + x), 1);
       mbar_init(bar(L::kOFull + x), 1);
     }
     mbar_init(bar(L::kDrain), 1);
+    mbar_init(bar(L::kDrain + 1), 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -171,79 +180,78 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int fills = issued > s ? (issued - 1 - s) / STAGES + 1 : 0;
         if (fills) wait_bar_drain(bar(L::kKVFull + s), (uint32_t)((fills - 1) & 1), status);
       }
-   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+   } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
+    // warp 1 issues tile A's MMAs, warp 2 tile B's: each waits only on its
+    // own softmax group, so one group's delay never holds the other's MMAs
     {
+      const int x = warp - 1;
       auto kv_wait = [&](int e) -> bool {
-        return wait_bar_w(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
-                          status);
+        if (!wait_bar_w(bar(L::kKVFull + e % STAGES), (uint32_t)((e / STAGES) & 1), abort_flag,
+                        status))
+          return false;
+        tc_fence_after();
+        return true;
       };
       // base descriptors, built once; MMAs add constant offsets
       const uint64_t dq0 = desc_kmajor(sb + L::Q);
       const uint64_t dkv_k = desc_kmajor(sb + L::KV);
       const uint64_t dkv_v = desc_mnmajor(sb + L::KV, 16384u);
-      auto qk = [&](int x, int e) {
+      const int U = 2 * n;  // half-steps: u = 2j + h covers keys [64h, 64h + 64) of tile j
+      // S_X slot h = Q_X (K_j rows [64h, 64h + 64))^T
+      auto qk = [&](int x, int u) {
+        const int j = u >> 1, h = u & 1;
         const uint64_t dq = desc_advance(dq0, (uint32_t)x * L::kTile);
-        const uint64_t dk = desc_advance(dkv_k, (uint32_t)(e % STAGES) * L::kTile);
+        const uint64_t dk =
+            desc_advance(dkv_k, (uint32_t)((2 * j) % STAGES) * L::kTile + (uint32_t)h * 8192u);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          mma_f16_ss_w(tmem + 128u * x, desc_advance(dq, off), desc_advance(dk, off), kIdescQK,
-                       kk > 0 ? 1u : 0u);
+          mma_f16_ss_w(tmem + 128u * x + 64u * h, desc_advance(dq, off), desc_advance(dk, off),
+                       kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto pv = [&](int x, int e, bool acc) {
-        const uint64_t dv = desc_advance(dkv_v, (uint32_t)(e % STAGES) * L::kTile);
+      // O_X += P_X(u) V_j rows [64h, 64h + 64), P_X(u) packed in slot h
+      auto pv = [&](int x, int u) {
+        const int j = u >> 1, h = u & 1;
+        const uint64_t dv = desc_advance(dkv_v, (uint32_t)((2 * j + 1) % STAGES) * L::kTile +
+                                                    (uint32_t)h * 8192u);
 #pragma unroll
-        for (int kk = 0; kk < kTN / 16; ++kk)
-          mma_f16_ts_w(tmem + 256u + 128u * x, tmem + 128u * x + 64u + 8u * kk,
-                       desc_advance(dv, (uint32_t)kk * 2048u), kIdescPV, (acc || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kHalf / 16; ++kk)
+          mma_f16_ts_w(tmem + 256u + 128u * x, tmem + 128u * x + 64u * h + 8u * kk,
+                       desc_advance(dv, (uint32_t)kk * 2048u), kIdescPV,
+                       (u > 0 || kk > 0) ? 1u : 0u);
       };
       bool ok = wait_bar_w(bar(L::kQFull), 0, abort_flag, status) && kv_wait(0);
       if (ok) {
-        tc_fence_after();
-        qk(0, 0);
-        tc_commit_w(bar(L::kSFull + 0));
-        qk(1, 0);
-        tc_commit_w(bar(L::kSFull + 1));
-        tc_commit_w(bar(L::kKVEmpty + 0));
-      }
-      for (int j = 1; ok && j < n; ++j) {
-        const int ev = 2 * j - 1, ek = 2 * j;
-        const uint32_t ph = (uint32_t)((j - 1) & 1);
-        if (!(kv_wait(ev) && kv_wait(ek))) { ok = false; break; }
-        if (!wait_bar_w(bar(L::kPFull + 0), ph, abort_flag, status)) { ok = false; break; }
-        tc_fence_after();
-        pv(0, ev, j > 1);
-        qk(0, ek);
-        tc_commit_w(bar(L::kSFull + 0));
-        if (!wait_bar_w(bar(L::kPFull + 1), ph, abort_flag, status)) { ok = false; break; }
-        tc_fence_after();
-        pv(1, ev, j > 1);
-        tc_commit_w(bar(L::kKVEmpty + ev % STAGES));
-        qk(1, ek);
-        tc_commit_w(bar(L::kSFull + 1));
-        tc_commit_w(bar(L::kKVEmpty + ek % STAGES));
-      }
-      if (ok) {
-        const int ev = 2 * n - 1;
-        const uint32_t ph = (uint32_t)((n - 1) & 1);
-        ok = kv_wait(ev) && wait_bar_w(bar(L::kPFull + 0), ph, abort_flag, status);
-        if (ok) {
-          tc_fence_after();
-          pv(0, ev, n > 1);
-          tc_commit_w(bar(L::kOFull + 0));
-          ok = wait_bar_w(bar(L::kPFull + 1), ph, abort_flag, status);
+        for (int h = 0; h < 2; ++h) {
+          qk(x, h);
+          tc_commit_w(bar(L::kSFull + 2 * x + h));
         }
-        if (ok) {
-          tc_fence_after();
-          pv(1, ev, n > 1);
-          tc_commit_w(bar(L::kOFull + 1));
-          tc_commit_w(bar(L::kKVEmpty + ev % STAGES));
+        tc_commit_w(bar(L::kKVEmpty + 0));  // K_0 fully read (one of the two arrivals)
+      }
+      for (int u = 0; ok && u < U; ++u) {
+        const int j = u >> 1, h = u & 1;
+        const bool more = u + 2 < U;
+        if (h == 0 && !(kv_wait(2 * j + 1) && (!more || kv_wait(2 * j + 2)))) break;  // V_j, K_{j+1}
+        if (!wait_bar_w(bar(L::kPFull + 2 * x + h), (uint32_t)((u >> 1) & 1), abort_flag,
+                        status))
+          break;
+        tc_fence_after();
+        pv(x, u);
+        tc_commit_w(bar(L::kPVDone + x));
+        if (more) {  // S_X(u+2) into the slot PV_X(u) has just read (MMAs run in order)
+          qk(x, u + 2);
+          tc_commit_w(bar(L::kSFull + 2 * x + h));
+        }
+        if (h == 1) {
+          tc_commit_w(bar(L::kKVEmpty + (2 * j + 1) % STAGES));            // V_j fully read
+          if (more) tc_commit_w(bar(L::kKVEmpty + (2 * j + 2) % STAGES));  // K_{j+1} too
         }
       }
-      tc_commit_w(bar(L::kDrain));
-      wait_bar_drain(bar(L::kDrain), 0, status);
+      tc_commit_w(bar(L::kOFull + x));
+      tc_commit_w(bar(L::kDrain + x));
+      wait_bar_drain(bar(L::kDrain + x), 0, status);
     }
    }
   } else {
@@ -254,36 +262,40 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int r = quarter * 32 + lane;
     const int row = row0 + x * kTM + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t t_s = tmem + lane_base + 128u * x;
-    const uint32_t t_p = t_s + 64u;
+    const uint32_t t_sx = tmem + lane_base + 128u * x;
     const uint32_t t_o = tmem + lane_base + 256u + 128u * x;
+    const int U = 2 * n;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    int32_t ent_next = col_idx[e0];
-    for (int j = 0; j < n; ++j) {
-      const int32_t ent = ent_next;
-      if (j + 1 < n) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
-      const int k0 = plan_index(ent) * kTN;
+    int32_t ent = 0, ent_next = col_idx[e0];
+    for (int u = 0; u < U; ++u) {
+      const int j = u >> 1, h = u & 1;
+      if (h == 0) {
+        ent = ent_next;
+        if (j + 1 < n) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
+      }
+      const int k0 = plan_index(ent) * kTN + kHalf * h;
       const bool partial = plan_partial(ent);
-      uint32_t vis[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-      const bool all_vis = block_all_visible(mp, row0 + x * kTM, kTM, k0, kTN, partial);
-      if (!all_vis) row_visibility<kTN>(vis, mp, row, k0, partial);
-      ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kSFull + x), (uint32_t)(j & 1), abort_flag, status));
+      uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
+      const bool all_vis = block_all_visible(mp, row0 + x * kTM, kTM, k0, kHalf, partial);
+      if (!all_vis) row_visibility<kHalf>(vis, mp, row, k0, partial);
+      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kSFull + 2 * x + h), (uint32_t)((u >> 1) & 1),
+                                            abort_flag, status));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kTN];
-#pragma unroll
-      for (int c = 0; c < kTN / 32; ++c) tmem_ld32(t_s + 32u * c, sv + 32 * c);
+      const uint32_t t_s = t_sx + 64u * h;
+      uint32_t sv[kHalf];
+      tmem_ld32(t_s, sv);
+      tmem_ld32(t_s + 32u, sv + 32);
       tmem_wait_ld();
       // row maximum of the raw scores; scale * log2(e) > 0 is applied after
       float rmax = -INFINITY;
       if (all_vis) {
 #pragma unroll
-        for (int c = 0; c < kTN; ++c) rmax = fmaxf(rmax, __uint_as_float(sv[c]));
+        for (int c = 0; c < kHalf; ++c) rmax = fmaxf(rmax, __uint_as_float(sv[c]));
       } else {
 #pragma unroll
-        for (int c = 0; c < kTN; ++c) {
+        for (int c = 0; c < kHalf; ++c) {
           const float v = ((vis[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(sv[c]) : -INFINITY;
           sv[c] = __float_as_uint(v);
           rmax = fmaxf(rmax, v);
@@ -292,7 +304,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float m_new = fmaxf(m_run, rmax * scale_log2);
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
       if (__any_sync(0xffffffffu, need)) {
-        // O_X already holds PV_X(j-1): it completed before S_X(j) did
+        // O_X holds PV_X(0 .. u-1) once PV_X(u-1) has completed; the S_X(u)
+        // barrier already implies PV_X(u-2), so this parity wait is exact
+        ok = __all_sync(0xffffffffu, u == 0 || wait_bar(bar(L::kPVDone + x),
+                                                        (uint32_t)((u - 1) & 1), abort_flag,
+                                                        status));
+        if (!ok) break;
+        tc_fence_after();
         const float alpha = need ? ex2(m_run - m_new) : 1.f;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -312,7 +330,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const bool dead = (m_run == -INFINITY);
       float rsum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kTN / 32; ++c) {
+      for (int c = 0; c < kHalf / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -323,12 +341,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           rsum += p0 + p1;
           pk[i] = pack2<T>(p0, p1);
         }
-        tmem_st16(t_p + 16u * c, pk);
+        tmem_st16(t_s + 16u * c, pk);
       }
       tmem_wait_st();
       l_run += rsum;
       tc_fence_before();
-      mbar_arrive(bar(L::kPFull + x));
+      mbar_arrive(bar(L::kPFull + 2 * x + h));
     }
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kOFull + x), 0, abort_flag, status));
     if (ok) {

@@ -484,10 +484,10 @@ struct DqLayout {
   static constexpr int kREmpty = 1 + kRing;          // [kRing]
   static constexpr int kSDFull = 1 + 2 * kRing;      // [2] S(j) and dP(j) written
   static constexpr int kDPFree = 3 + 2 * kRing;      // compute read dP(j)
-  static constexpr int kPReady = 4 + 2 * kRing;      // compute wrote dS(j)
-  static constexpr int kDone = 5 + 2 * kRing;
-  static constexpr int kDrain = 6 + 2 * kRing;
-  static constexpr int kNumBars = 7 + 2 * kRing;
+  static constexpr int kPReady = 4 + 2 * kRing;      // [2] compute wrote dS(j) into S[j&1]
+  static constexpr int kDone = 6 + 2 * kRing;
+  static constexpr int kDrain = 7 + 2 * kRing;
+  static constexpr int kNumBars = 8 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kAlloc = MISC + 16 + 1024;
 };
@@ -542,6 +542,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kSDFull + 1), 1);
     mbar_init(bar(L::kDPFree), 256);
     mbar_init(bar(L::kPReady), 256);
+    mbar_init(bar(L::kPReady + 1), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
@@ -638,7 +639,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_commit_w(bar(L::kSDFull + ((j + 1) & 1)));
           tc_commit_w(bar(L::kREmpty + (2 * j + 2) % kRing));
         }
-        if (!wait_bar_w(bar(L::kPReady), (uint32_t)(j & 1), abort_flag, status)) {
+        if (!wait_bar_w(bar(L::kPReady + (j & 1)), (uint32_t)((j >> 1) & 1), abort_flag,
+                        status)) {
           ok = false;
           break;
         }
@@ -723,7 +725,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_st32(t_s, ds2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(L::kPReady));
+      mbar_arrive(bar(L::kPReady + (j & 1)));
     }
     // epilogue: dQ columns [64*grp, 64*grp + 64) staged in Q's buffer
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
