@@ -76,7 +76,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled, into this CTA's own shared memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y, int z) {
