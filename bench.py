@@ -1,7 +1,7 @@
 """Benchmark: StreamingLLM block-sparse attention on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload all|fwdbwd|fwd|decode]
+                    [--workload all|fwdbwd|fwd|decode|fx]
 
 Headline (``value``): BASELINE config 2 -- sparse prefill forward+backward,
 B=4, H=32, N=16384, D=128, bf16, S=4, W=2048, BM=BN=128 -- as kept-block
@@ -41,6 +41,8 @@ import torch  # noqa: E402
 CFG2 = dict(B=4, H=32, N=16384, D=128, S=4, W=2048, BM=128, BN=128, dtype=torch.bfloat16)
 CFG3 = dict(B=1, H=32, N=131072, D=128, S=4, W=4096, BM=128, BN=128, dtype=torch.float16)
 CFG4 = dict(B=64, H=32, N=100001, D=128, S=4, W=2048, BM=1, BN=64, dtype=torch.float16)
+CFG5 = dict(B=2, N=32768, hidden=4096, layers=8, H=32, D=128, mlp=11008, vocab=32000, S=4,
+            W=2048, BM=64, BN=64, dtype=torch.bfloat16)
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -369,6 +371,69 @@ def bench_decode(dist, args, pk, src):
                 launches=launches)
 
 
+def bench_fx(dist, args, pk, src):
+    """Config 5: the Llama-style decoder rewritten by the FX pass, one
+    forward + backward step (loss = cross entropy on random targets; no
+    optimizer step, as the config specifies).  Reports tokens/s of the whole
+    step and the share of the step spent in this library's kernels."""
+    import torch.nn.functional as F  # noqa: N812
+
+    import sparse_triton_kernel as stk
+    from fx_compiler_pass import BlockSparseAttentionInjector, InjectionConfig, LlamaStyleDecoder
+    cfg = dict(CFG5)
+    if args.fx_layers > 0:
+        cfg["layers"] = args.fx_layers
+    torch.manual_seed(1234 + dist.rank)
+    model = LlamaStyleDecoder(vocab=cfg["vocab"], hidden=cfg["hidden"], n_layers=cfg["layers"],
+                              n_heads=cfg["H"], mlp=cfg["mlp"], max_seq=cfg["N"],
+                              device="cuda", dtype=cfg["dtype"])
+    icfg = InjectionConfig(seq_len_q=cfg["N"], seq_len_kv=cfg["N"], head_dim=cfg["D"],
+                           streaming=stk.StreamingMaskSpec(cfg["S"], cfg["W"]),
+                           block_m=cfg["BM"], block_n=cfg["BN"])
+    gm = BlockSparseAttentionInjector(icfg).transform(model).to("cuda")
+    n_inj = sum(1 for n in gm.graph.nodes
+                if n.op == "call_module" and str(n.target).startswith("_triton_attn_"))
+    g = torch.Generator(device="cuda").manual_seed(dist.rank)
+    ids = torch.randint(0, cfg["vocab"], (cfg["B"], cfg["N"]), generator=g, device="cuda")
+    tgt = torch.randint(0, cfg["vocab"], (cfg["B"], cfg["N"]), generator=g, device="cuda")
+    params = list(model.parameters())
+
+    def step():
+        for p in params:
+            p.grad = None
+        logits = gm(ids)
+        loss = F.cross_entropy(logits.view(-1, cfg["vocab"]).float(), tgt.view(-1))
+        loss.backward()
+        return loss
+
+    steps = max(2, min(args.steps, 3))
+    ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
+    loss = float(step().item())
+    ours_ms = sum(v[0] for v in per_kernel.values())
+    nnz = int(stk.make_streaming_mask(cfg["N"], cfg["N"], stk.StreamingMaskSpec(cfg["S"], cfg["W"]),
+                                      cfg["BM"], cfg["BN"], device="cuda").sum().item())
+    attn_flops = 3.5 * nnz * cfg["B"] * cfg["H"] * 4 * cfg["BM"] * cfg["BN"] * cfg["D"] * \
+        cfg["layers"]
+    n_params = sum(p.numel() for p in params)
+    tokens = cfg["B"] * cfg["N"]
+    res = {"tokens_per_s": round(tokens * dist.world * steps / (ms / 1e3), 1),
+           "ms_per_step": round(ms / steps, 2), "layers": cfg["layers"],
+           "injected_modules": n_inj, "kept_blocks": nnz, "loss": round(loss, 4),
+           "attention_ms_per_step": round(ours_ms / steps, 2),
+           "attention_share": round(ours_ms / ms, 4),
+           "attention_tflops": round(attn_flops * steps / (ours_ms / 1e3) / 1e12, 1),
+           "model_tflops_est": round((6 * n_params * tokens + attn_flops) * steps /
+                                     (ms / 1e3) / 1e12, 1),
+           "params": n_params, "gpu_launches": launches,
+           "per_kernel_ms": {k: round(v[0] / steps, 3) for k, v in per_kernel.items()},
+           "config": "8-layer Llama-style decoder (hidden 4096, 32 heads, D=128, SwiGLU "
+                     "11008, RMSNorm, RoPE), bf16 random init, B=2 N=32768, SDPA(is_causal) "
+                     f"rewritten by the FX pass, S=4 W=2048 BM=BN={cfg['BM']}"}
+    del gm, model, params, ids, tgt
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (upstream eager masked attention, oracle port)
 # ---------------------------------------------------------------------------
@@ -451,7 +516,10 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["all", "fwdbwd", "fwd", "decode"], default="all")
+    ap.add_argument("--workload", choices=["all", "fwdbwd", "fwd", "decode", "fx"],
+                    default="all")
+    ap.add_argument("--fx-layers", type=int, default=0,
+                    help="override the layer count of the config-5 model (small runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
                     help="override the per-rank head count (small cases for profiling)")
@@ -497,6 +565,14 @@ def main():
         if args.workload == "decode":
             line.update({"metric": "decode KV GB/s", "unit": "GB/s", "value": extra[
                 "cfg4_decode"]["value"], "roofline": r["roofline"], "dtype": "fp16"})
+    if args.workload == "fx":
+        r = bench_fx(dist, args, pk, src)
+        extra["cfg5_fx_end_to_end"] = r
+        line.update({"metric": "FX end-to-end tokens/s (fwd+bwd)", "unit": "tokens/s",
+                     "value": r["tokens_per_s"], "ms_per_step": r["ms_per_step"],
+                     "gpu_launches": r["gpu_launches"], "config": {
+                         "workload": r["config"], "global_batch": CFG5["B"] * dist.world,
+                         "seq_len": CFG5["N"], "parallelism": f"replicas x{dist.world}"}})
     line["extra"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and \
             args.workload in ("all", "fwdbwd"):

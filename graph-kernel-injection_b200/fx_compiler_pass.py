@@ -80,6 +80,102 @@ class SingleLayerTransformer(nn.Module):
         return self.out_proj(self._merge(o))
 
 
+class _RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6, **kw) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim, **kw))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return y.to(x.dtype) * self.weight
+
+
+def _rope_rows(table: torch.Tensor, n: int, dtype: torch.dtype) -> torch.Tensor:
+    """First ``n`` rows of a RoPE cos/sin table (a leaf of the traced graph)."""
+    return table[:n].to(dtype)
+
+
+fx.wrap("_rope_rows")
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    half = x.shape[-1] // 2
+    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+
+class _LlamaAttention(nn.Module):
+    def __init__(self, hidden: int, n_heads: int, max_seq: int, theta: float, **kw) -> None:
+        super().__init__()
+        self.n_heads, self.head_dim = n_heads, hidden // n_heads
+        self.q_proj = nn.Linear(hidden, hidden, bias=False, **kw)
+        self.k_proj = nn.Linear(hidden, hidden, bias=False, **kw)
+        self.v_proj = nn.Linear(hidden, hidden, bias=False, **kw)
+        self.o_proj = nn.Linear(hidden, hidden, bias=False, **kw)
+        dev = kw.get("device")
+        inv = 1.0 / theta ** (torch.arange(0, self.head_dim, 2, device=dev).float() / self.head_dim)
+        ang = torch.outer(torch.arange(max_seq, device=dev).float(), inv)
+        ang = torch.cat((ang, ang), dim=-1)
+        self.register_buffer("cos", ang.cos(), persistent=False)
+        self.register_buffer("sin", ang.sin(), persistent=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        b, n, _ = x.shape
+        q = self.q_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
+        cos = _rope_rows(self.cos, n, q.dtype)
+        sin = _rope_rows(self.sin, n, q.dtype)
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return self.o_proj(o.transpose(1, 2).reshape(b, n, self.n_heads * self.head_dim))
+
+
+class _LlamaBlock(nn.Module):
+    def __init__(self, hidden: int, n_heads: int, mlp: int, max_seq: int, theta: float,
+                 **kw) -> None:
+        super().__init__()
+        self.attn_norm = _RMSNorm(hidden, **kw)
+        self.attn = _LlamaAttention(hidden, n_heads, max_seq, theta, **kw)
+        self.mlp_norm = _RMSNorm(hidden, **kw)
+        self.gate = nn.Linear(hidden, mlp, bias=False, **kw)
+        self.up = nn.Linear(hidden, mlp, bias=False, **kw)
+        self.down = nn.Linear(mlp, hidden, bias=False, **kw)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = x + self.attn(self.attn_norm(x))
+        h = self.mlp_norm(x)
+        return x + self.down(F.silu(self.gate(h)) * self.up(h))
+
+
+class LlamaStyleDecoder(nn.Module):
+    """Llama-style decoder (RMSNorm, RoPE, SwiGLU MLP, untied LM head) whose
+    attention is ``F.scaled_dot_product_attention(..., is_causal=True)`` on
+    ``[B, H, N, D]`` transposed views -- the SDPA shape the pass rewrites.
+    ``forward(ids) -> logits``.  Keyword arguments ``device`` / ``dtype``
+    place and type every parameter at construction."""
+
+    def __init__(self, vocab: int = 32000, hidden: int = 4096, n_layers: int = 8,
+                 n_heads: int = 32, mlp: int = 11008, max_seq: int = 32768,
+                 rope_theta: float = 10000.0, device=None, dtype=None) -> None:
+        super().__init__()
+        kw = {"device": device, "dtype": dtype}
+        self.embed = nn.Embedding(vocab, hidden, **kw)
+        self.layers = nn.ModuleList(
+            _LlamaBlock(hidden, n_heads, mlp, max_seq, rope_theta, **kw)
+            for _ in range(n_layers))
+        self.norm = _RMSNorm(hidden, **kw)
+        self.lm_head = nn.Linear(hidden, vocab, bias=False, **kw)
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        x = self.embed(ids)
+        for layer in self.layers:
+            x = layer(x)
+        return self.lm_head(self.norm(x))
+
+
 # ---------------------------------------------------------------------------
 # The installed module
 # ---------------------------------------------------------------------------

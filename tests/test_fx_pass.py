@@ -225,3 +225,19 @@ def test_original_model_untouched_and_printer():
 def test_standard_attention_rejects_bad_dim():
     with pytest.raises(ValueError):
         StandardAttention(0)
+
+
+def test_llama_style_decoder_rewritten():
+    """cfg5's model shape (RMSNorm, RoPE on transposed views, SDPA
+    is_causal=True, SwiGLU) in miniature: every layer's SDPA becomes one
+    injected module and all of them share one mask buffer."""
+    from fx_compiler_pass import LlamaStyleDecoder
+    model = LlamaStyleDecoder(vocab=100, hidden=64, n_layers=3, n_heads=4, mlp=128, max_seq=64)
+    gm = BlockSparseAttentionInjector(cfg()).transform(model)
+    assert sdpa_calls(gm) == 0 and injected(gm) == 3
+    mods = [gm.get_submodule(f"_triton_attn_{i}") for i in range(3)]
+    assert all(m.block_mask is mods[0].block_mask for m in mods)
+    assert all(m.is_causal and m.sink_size == 4 and m.window_size == 16 for m in mods)
+    assert mods[0].softmax_scale == pytest.approx(0.25)
+    ids = torch.randint(0, 100, (1, 64))
+    assert model(ids).shape == (1, 64, 100)  # the original model is untouched and runs
