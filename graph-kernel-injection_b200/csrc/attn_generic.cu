@@ -43,15 +43,16 @@ __device__ __forceinline__ A warp_sum(A x) {
   return x;
 }
 
-// Load `rows` rows of a [N, D] slice starting at row r0 into smem (row
-// stride `ld`), converting to the accumulator type; rows >= n are zero.
+// Load `rows` rows of an [N, D] slice (global row stride `sn` elements)
+// starting at row r0 into smem (row stride `ld`), converting to the
+// accumulator type; rows >= n are zero.
 template <typename T, typename A>
-__device__ __forceinline__ void load_rows(A* dst, int ld, const T* src, int r0, int rows,
-                                          int n, int D) {
+__device__ __forceinline__ void load_rows(A* dst, int ld, const T* src, int64_t sn, int r0,
+                                          int rows, int n, int D) {
   for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
     int r = i / D, d = i - r * D;
     int gr = r0 + r;
-    dst[r * ld + d] = gr < n ? Elem<T>::to(src[(size_t)gr * D + d]) : A(0);
+    dst[r * ld + d] = gr < n ? Elem<T>::to(src[(int64_t)gr * sn + d]) : A(0);
   }
 }
 
@@ -61,7 +62,7 @@ __device__ __forceinline__ void load_rows(A* dst, int ld, const T* src, int r0, 
 template <typename T, int DPL>
 __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    T* __restrict__ o, float* __restrict__ lse, int D, double scale_f, MaskParams mp,
+    T* __restrict__ o, float* __restrict__ lse, int D, double scale_f, MaskParams mp, Views vw,
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -72,11 +73,11 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
   const size_t bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
-  const T* qb = q + bh * (size_t)mp.n_q * D;
-  const T* kb = k + bh * (size_t)mp.n_kv * D;
-  const T* vb = v + bh * (size_t)mp.n_kv * D;
+  const T* qb = q + vw.at(vw.q, (int)bh, 0);
+  const T* kb = k + vw.at(vw.k, (int)bh, 0);
+  const T* vb = v + vw.at(vw.v, (int)bh, 0);
   const int row0 = ti * kRows;
-  load_rows<T, A>(Qs, D, qb, row0, kRows, mp.n_q, D);
+  load_rows<T, A>(Qs, D, qb, vw.q.n, row0, kRows, mp.n_q, D);
 
   A m[4], l[4], acc[4][DPL];
 #pragma unroll
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
     const bool partial = plan_partial(ent);
     const int k0 = tj * kKeys;
     __syncthreads();
-    load_rows<T, A>(Ks, D + 1, kb, k0, kKeys, mp.n_kv, D);
-    load_rows<T, A>(Vs, D, vb, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Ks, D + 1, kb, vw.k.n, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Vs, D, vb, vw.v.n, k0, kKeys, mp.n_kv, D);
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
       m[r] = m_new;
     }
   }
-  T* ob = o + bh * (size_t)mp.n_q * D;
+  T* ob = o + vw.at(vw.o, (int)bh, 0);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int row = row0 + warp * 4 + r;
@@ -145,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
       const int d = lane + 32 * i;
-      if (d < D) ob[(size_t)row * D + d] = Elem<T>::from(valid ? acc[r][i] * inv : A(0));
+      if (d < D) ob[(int64_t)row * vw.o.n + d] = Elem<T>::from(valid ? acc[r][i] * inv : A(0));
     }
     if (lane == 0)
       lse[bh * mp.n_q + row] = valid ? (float)(m[r] + acc_log<A>(l[r])) : 0.0f;
@@ -155,19 +156,64 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
 // ---------------------------------------------------------------------------
 // Backward: Delta = rowsum(O * dO)
 // ---------------------------------------------------------------------------
+// One block row per (row tile, bh): no index division per row.  When a row
+// is a whole number of 16-byte vectors (D * sizeof(T) % 16 == 0, at most 32
+// of them), `g` = D / vec lanes share a row with one vector load each and
+// 32 / g rows run per warp; otherwise a warp takes a row with scalar loads.
 template <typename T>
 __global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ dout,
-                             float* __restrict__ delta, int64_t rows, int D) {
+                             float* __restrict__ delta, int n_q, int D, int g, Views vw) {
   using A = typename Elem<T>::acc;
-  const int lane = threadIdx.x & 31;
-  int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  for (; r < rows; r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+  constexpr int kVec = 16 / sizeof(T);
+  const int bh = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const T* ob = o + vw.at(vw.o, bh, 0);
+  const T* gb = dout + vw.at(vw.dout, bh, 0);
+  float* db = delta + (int64_t)bh * n_q;
+  if (g > 0) {
+    const int per_warp = 32 / g;
+    const int row = (blockIdx.x * (blockDim.x >> 5) + warp) * per_warp + lane / g;
+    const int sub = lane % g;
+    A s = 0;
+    if (row < n_q) {
+      const uint4 a = *reinterpret_cast<const uint4*>(ob + (int64_t)row * vw.o.n + sub * kVec);
+      const uint4 b = *reinterpret_cast<const uint4*>(gb + (int64_t)row * vw.dout.n + sub * kVec);
+      const T* ta = reinterpret_cast<const T*>(&a);
+      const T* tb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) s += Elem<T>::to(ta[i]) * Elem<T>::to(tb[i]);
+    }
+    for (int off = g >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (row < n_q && sub == 0) db[row] = (float)s;
+  } else {
+    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (row >= n_q) return;
     A s = 0;
     for (int d = lane; d < D; d += 32)
-      s += Elem<T>::to(o[r * D + d]) * Elem<T>::to(dout[r * D + d]);
+      s += Elem<T>::to(ob[(int64_t)row * vw.o.n + d]) * Elem<T>::to(gb[(int64_t)row * vw.dout.n + d]);
     s = warp_sum(s);
-    if (lane == 0) delta[r] = (float)s;
+    if (lane == 0) db[row] = (float)s;
   }
+}
+
+// Launch of delta_kernel for any dtype; vector loads when every row start
+// is 16-byte aligned.
+template <typename T>
+int launch_delta(const void* o, const void* dout, float* delta, int BH, int n_q, int D,
+                 const Views& vw, cudaStream_t s) {
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec_ok = D % kVec == 0 && D / kVec <= 32 && ((D / kVec) & (D / kVec - 1)) == 0 &&
+                      ((uintptr_t)o % 16 == 0) && ((uintptr_t)dout % 16 == 0) &&
+                      vw.o.n % kVec == 0 && vw.o.h % kVec == 0 && vw.o.b % kVec == 0 &&
+                      vw.dout.n % kVec == 0 && vw.dout.h % kVec == 0 && vw.dout.b % kVec == 0;
+  const int g = vec_ok ? D / kVec : 0;
+  const int rows_per_block = 8 * (g > 0 ? 32 / g : 1);
+  dim3 grid(ceil_div_i(n_q, rows_per_block), BH);
+  {
+    LaunchScope ls("delta_kernel", s);
+    delta_kernel<T><<<grid, 256, 0, s>>>((const T*)o, (const T*)dout, delta, n_q, D, g, vw);
+  }
+  return check_launch("delta_kernel");
 }
 
 // ---------------------------------------------------------------------------
@@ -178,7 +224,7 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const T* __restrict__ dout, const float* __restrict__ lse,
     const float* __restrict__ delta, T* __restrict__ dq, int D, double scale_f, MaskParams mp,
-    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+    Views vw, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   A* Qs = reinterpret_cast<A*>(smem_raw);   // [kRows][D]
@@ -189,11 +235,11 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
   const size_t bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
-  const T* kb = k + bh * (size_t)mp.n_kv * D;
-  const T* vb = v + bh * (size_t)mp.n_kv * D;
+  const T* kb = k + vw.at(vw.k, (int)bh, 0);
+  const T* vb = v + vw.at(vw.v, (int)bh, 0);
   const int row0 = ti * kRows;
-  load_rows<T, A>(Qs, D, q + bh * (size_t)mp.n_q * D, row0, kRows, mp.n_q, D);
-  load_rows<T, A>(dOs, D, dout + bh * (size_t)mp.n_q * D, row0, kRows, mp.n_q, D);
+  load_rows<T, A>(Qs, D, q + vw.at(vw.q, (int)bh, 0), vw.q.n, row0, kRows, mp.n_q, D);
+  load_rows<T, A>(dOs, D, dout + vw.at(vw.dout, (int)bh, 0), vw.dout.n, row0, kRows, mp.n_q, D);
   A lse_r[4], del_r[4], acc[4][DPL];
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -210,8 +256,8 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
     const bool partial = plan_partial(ent);
     const int k0 = tj * kKeys;
     __syncthreads();
-    load_rows<T, A>(Ks, D + 1, kb, k0, kKeys, mp.n_kv, D);
-    load_rows<T, A>(Vs, D + 1, vb, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Ks, D + 1, kb, vw.k.n, k0, kKeys, mp.n_kv, D);
+    load_rows<T, A>(Vs, D + 1, vb, vw.v.n, k0, kKeys, mp.n_kv, D);
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -250,7 +296,7 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
       }
     }
   }
-  T* dqb = dq + bh * (size_t)mp.n_q * D;
+  T* dqb = dq + vw.at(vw.dq, (int)bh, 0);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int row = row0 + warp * 4 + r;
@@ -258,7 +304,7 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
       const int d = lane + 32 * i;
-      if (d < D) dqb[(size_t)row * D + d] = Elem<T>::from(acc[r][i]);
+      if (d < D) dqb[(int64_t)row * vw.dq.n + d] = Elem<T>::from(acc[r][i]);
     }
   }
 }
@@ -271,7 +317,7 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const T* __restrict__ dout, const float* __restrict__ lse,
     const float* __restrict__ delta, T* __restrict__ dk, T* __restrict__ dv, int D,
-    double scale_f, MaskParams mp, const int32_t* __restrict__ col_ptr,
+    double scale_f, MaskParams mp, Views vw, const int32_t* __restrict__ col_ptr,
     const int32_t* __restrict__ row_idx) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -285,11 +331,11 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
   const size_t bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
-  const T* qb = q + bh * (size_t)mp.n_q * D;
-  const T* gb = dout + bh * (size_t)mp.n_q * D;
+  const T* qb = q + vw.at(vw.q, (int)bh, 0);
+  const T* gb = dout + vw.at(vw.dout, (int)bh, 0);
   const int key0 = tj * kKvKeys;
-  load_rows<T, A>(Ks, D, k + bh * (size_t)mp.n_kv * D, key0, kKvKeys, mp.n_kv, D);
-  load_rows<T, A>(Vs, D, v + bh * (size_t)mp.n_kv * D, key0, kKvKeys, mp.n_kv, D);
+  load_rows<T, A>(Ks, D, k + vw.at(vw.k, (int)bh, 0), vw.k.n, key0, kKvKeys, mp.n_kv, D);
+  load_rows<T, A>(Vs, D, v + vw.at(vw.v, (int)bh, 0), vw.v.n, key0, kKvKeys, mp.n_kv, D);
   A adk[4][DPL], adv[4][DPL];
 #pragma unroll
   for (int c = 0; c < 4; ++c)
@@ -302,8 +348,8 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     const bool partial = plan_partial(ent);
     const int r0 = ti * kKvRows;
     __syncthreads();
-    load_rows<T, A>(Qs, D + 1, qb, r0, kKvRows, mp.n_q, D);
-    load_rows<T, A>(dOs, D + 1, gb, r0, kKvRows, mp.n_q, D);
+    load_rows<T, A>(Qs, D + 1, qb, vw.q.n, r0, kKvRows, mp.n_q, D);
+    load_rows<T, A>(dOs, D + 1, gb, vw.dout.n, r0, kKvRows, mp.n_q, D);
     for (int i = threadIdx.x; i < kKvRows; i += blockDim.x) {
       const int row = r0 + i;
       Ls[i] = row < mp.n_q ? (A)lse[bh * mp.n_q + row] : A(0);
@@ -354,8 +400,8 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
       }
     }
   }
-  T* dkb = dk + bh * (size_t)mp.n_kv * D;
-  T* dvb = dv + bh * (size_t)mp.n_kv * D;
+  T* dkb = dk + vw.at(vw.dk, (int)bh, 0);
+  T* dvb = dv + vw.at(vw.dv, (int)bh, 0);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const int key = key0 + warp * 4 + c;
@@ -364,8 +410,8 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     for (int i = 0; i < DPL; ++i) {
       const int d = lane + 32 * i;
       if (d < D) {
-        dkb[(size_t)key * D + d] = Elem<T>::from(adk[c][i]);
-        dvb[(size_t)key * D + d] = Elem<T>::from(adv[c][i]);
+        dkb[(int64_t)key * vw.dk.n + d] = Elem<T>::from(adk[c][i]);
+        dvb[(int64_t)key * vw.dv.n + d] = Elem<T>::from(adv[c][i]);
       }
     }
   }
@@ -394,7 +440,7 @@ int set_smem(K kernel, size_t bytes) {
 
 template <typename T, int DPL>
 int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH,
-               int D, double scale, const MaskParams& mp, const int32_t* row_ptr,
+               int D, double scale, const MaskParams& mp, const Views& vw, const int32_t* row_ptr,
                const int32_t* col_idx, cudaStream_t s) {
   auto kern = fwd_generic_kernel<T, DPL>;
   size_t sm = fwd_smem<T>(D);
@@ -403,7 +449,7 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   {
     LaunchScope ls("fwd_generic_kernel", s);
     kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, D,
-                                    scale, mp, row_ptr, col_idx);
+                                    scale, mp, vw, row_ptr, col_idx);
   }
   return check_launch("fwd_generic_kernel");
 }
@@ -411,16 +457,10 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
 template <typename T, int DPL>
 int launch_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
                const void* dout, void* dq, void* dk, void* dv, float* delta, int BH, int D,
-               double scale, const MaskParams& mp, const int32_t* dq_row_ptr,
+               double scale, const MaskParams& mp, const Views& vw, const int32_t* dq_row_ptr,
                const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
                const int32_t* kv_row_idx, cudaStream_t s) {
-  const int64_t rows = (int64_t)BH * mp.n_q;
-  int dgrid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 64);
-  {
-    LaunchScope ls("delta_kernel", s);
-    delta_kernel<T><<<dgrid, 256, 0, s>>>((const T*)o, (const T*)dout, delta, rows, D);
-  }
-  if (int rc = check_launch("delta_kernel")) return rc;
+  if (int rc = launch_delta<T>(o, dout, delta, BH, mp.n_q, D, vw, s)) return rc;
   {
     auto kern = dkdv_generic_kernel<T, DPL>;
     size_t sm = dkdv_smem<T>(D);
@@ -429,8 +469,8 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
     {
       LaunchScope ls("dkdv_generic_kernel", s);
       kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
-                                      lse, delta, (T*)dk, (T*)dv, D, scale, mp, kv_col_ptr,
-                                      kv_row_idx);
+                                      lse, delta, (T*)dk, (T*)dv, D, scale, mp, vw,
+                                      kv_col_ptr, kv_row_idx);
     }
     if (int rc = check_launch("dkdv_generic_kernel")) return rc;
   }
@@ -442,7 +482,8 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
     {
       LaunchScope ls("dq_generic_kernel", s);
       kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
-                                      lse, delta, (T*)dq, D, scale, mp, dq_row_ptr, dq_col_idx);
+                                      lse, delta, (T*)dq, D, scale, mp, vw, dq_row_ptr,
+                                      dq_col_idx);
     }
     return check_launch("dq_generic_kernel");
   }
@@ -450,43 +491,40 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
 
 template <typename T>
 int dispatch_fwd(int D, const void* q, const void* k, const void* v, void* o, float* lse,
-                 int BH, double scale, const MaskParams& mp, const int32_t* rp,
+                 int BH, double scale, const MaskParams& mp, const Views& vw, const int32_t* rp,
                  const int32_t* ci, cudaStream_t s) {
-  if (D <= 32) return launch_fwd<T, 1>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
-  if (D <= 64) return launch_fwd<T, 2>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
-  if (D <= 128) return launch_fwd<T, 4>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
-  return launch_fwd<T, 8>(q, k, v, o, lse, BH, D, scale, mp, rp, ci, s);
+  if (D <= 32) return launch_fwd<T, 1>(q, k, v, o, lse, BH, D, scale, mp, vw, rp, ci, s);
+  if (D <= 64) return launch_fwd<T, 2>(q, k, v, o, lse, BH, D, scale, mp, vw, rp, ci, s);
+  if (D <= 128) return launch_fwd<T, 4>(q, k, v, o, lse, BH, D, scale, mp, vw, rp, ci, s);
+  return launch_fwd<T, 8>(q, k, v, o, lse, BH, D, scale, mp, vw, rp, ci, s);
 }
 
 template <typename T>
 int dispatch_bwd(int D, const void* q, const void* k, const void* v, const void* o,
                  const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                 int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
-                 const int32_t* c, const int32_t* d, cudaStream_t s) {
+                 int BH, double scale, const MaskParams& mp, const Views& vw, const int32_t* a,
+                 const int32_t* b, const int32_t* c, const int32_t* d, cudaStream_t s) {
   if (D <= 32)
-    return launch_bwd<T, 1>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+    return launch_bwd<T, 1>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, vw, a, b, c, d, s);
   if (D <= 64)
-    return launch_bwd<T, 2>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+    return launch_bwd<T, 2>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, vw, a, b, c, d, s);
   if (D <= 128)
-    return launch_bwd<T, 4>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
-  return launch_bwd<T, 8>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, a, b, c, d, s);
+    return launch_bwd<T, 4>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, vw, a, b, c, d, s);
+  return launch_bwd<T, 8>(q, k, v, o, lse, dout, dq, dk, dv, delta, BH, D, scale, mp, vw, a, b, c, d, s);
 }
 
 }  // namespace
 
 // Delta = rowsum(O * dO) in fp32 (used by the tensor-core backward too).
-int generic_delta(int dtype, const void* o, const void* dout, float* delta, int64_t rows, int D,
-                  cudaStream_t s) {
-  const int grid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 64);
-  LaunchScope ls("delta_kernel", s);
+int generic_delta(int dtype, const void* o, const void* dout, float* delta, int BH, int n_q,
+                  int D, const Views& vw, cudaStream_t s) {
   switch (dtype) {
-    case SBFA_F16: delta_kernel<__half><<<grid, 256, 0, s>>>((const __half*)o, (const __half*)dout, delta, rows, D); break;
-    case SBFA_BF16: delta_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, rows, D); break;
-    case SBFA_F32: delta_kernel<float><<<grid, 256, 0, s>>>((const float*)o, (const float*)dout, delta, rows, D); break;
-    case SBFA_F64: delta_kernel<double><<<grid, 256, 0, s>>>((const double*)o, (const double*)dout, delta, rows, D); break;
-    default: return fail(SBFA_ERR_INVALID, "unknown dtype");
+    case SBFA_F16: return launch_delta<__half>(o, dout, delta, BH, n_q, D, vw, s);
+    case SBFA_BF16: return launch_delta<__nv_bfloat16>(o, dout, delta, BH, n_q, D, vw, s);
+    case SBFA_F32: return launch_delta<float>(o, dout, delta, BH, n_q, D, vw, s);
+    case SBFA_F64: return launch_delta<double>(o, dout, delta, BH, n_q, D, vw, s);
   }
-  return check_launch("delta_kernel");
+  return fail(SBFA_ERR_INVALID, "unknown dtype");
 }
 
 // Entry points used by capi.cu.
@@ -503,30 +541,31 @@ bool generic_supports(int dtype, int64_t D) {
 }
 
 int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o,
-                float* lse, int BH, double scale, const MaskParams& mp, const int32_t* rp,
-                const int32_t* ci, cudaStream_t s) {
+                float* lse, int BH, double scale, const MaskParams& mp, const Views& vw,
+                const int32_t* rp, const int32_t* ci, cudaStream_t s) {
   switch (dtype) {
-    case SBFA_F16: return dispatch_fwd<__half>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
-    case SBFA_BF16: return dispatch_fwd<__nv_bfloat16>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
-    case SBFA_F32: return dispatch_fwd<float>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
-    case SBFA_F64: return dispatch_fwd<double>(D, q, k, v, o, lse, BH, scale, mp, rp, ci, s);
+    case SBFA_F16: return dispatch_fwd<__half>(D, q, k, v, o, lse, BH, scale, mp, vw, rp, ci, s);
+    case SBFA_BF16:
+      return dispatch_fwd<__nv_bfloat16>(D, q, k, v, o, lse, BH, scale, mp, vw, rp, ci, s);
+    case SBFA_F32: return dispatch_fwd<float>(D, q, k, v, o, lse, BH, scale, mp, vw, rp, ci, s);
+    case SBFA_F64: return dispatch_fwd<double>(D, q, k, v, o, lse, BH, scale, mp, vw, rp, ci, s);
   }
   return fail(SBFA_ERR_INVALID, "unknown dtype");
 }
 
 int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
-                const int32_t* c, const int32_t* d, cudaStream_t s) {
+                int BH, double scale, const MaskParams& mp, const Views& vw, const int32_t* a,
+                const int32_t* b, const int32_t* c, const int32_t* d, cudaStream_t s) {
   switch (dtype) {
     case SBFA_F16:
-      return dispatch_bwd<__half>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+      return dispatch_bwd<__half>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, vw, a, b, c, d, s);
     case SBFA_BF16:
-      return dispatch_bwd<__nv_bfloat16>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+      return dispatch_bwd<__nv_bfloat16>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, vw, a, b, c, d, s);
     case SBFA_F32:
-      return dispatch_bwd<float>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+      return dispatch_bwd<float>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, vw, a, b, c, d, s);
     case SBFA_F64:
-      return dispatch_bwd<double>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, a, b, c, d, s);
+      return dispatch_bwd<double>(D, q, k, v, o, lse, dout, dq, dk, dv, delta, BH, scale, mp, vw, a, b, c, d, s);
   }
   return fail(SBFA_ERR_INVALID, "unknown dtype");
 }

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
                   T* __restrict__ o, float* __restrict__ lse, float scale_log2, MaskParams mp,
                   const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
-                  int* status) {
+                  int heads, Strides3 so, int* status) {
   using L = FwdLayout<D, STAGES>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescQK = idesc_f16(kBF16, kTM, kHalf, false, false);
@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x;
   const int bh = blockIdx.y;
+  const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
   const int row0 = pair * kPair * kTM;
   const int e0 = row_ptr[pair];
   const int n = row_ptr[pair + 1] - e0;
@@ -108,7 +109,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int rr = idx / (D / 8), cc = idx % (D / 8);
       const int row = row0 + rr;
       if (row < mp.n_q)
-        reinterpret_cast<uint4*>(o + ((size_t)bh * mp.n_q + row) * D)[cc] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(o + bb * so.b + hh * so.h + (int64_t)row * so.n)[cc] =
+            make_uint4(0, 0, 0, 0);
     }
     for (int rr = threadIdx.x; rr < kPair * kTM; rr += blockDim.x) {
       const int row = row0 + rr;
@@ -152,8 +154,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_expect_tx(bar(L::kQFull), kPair * L::kTile);
       for (int x = 0; x < kPair; ++x)
         for (int r = 0; r < kBoxes; ++r)
-          tma_load_3d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
-                      row0 + x * kTM, bh);
+          tma_load_4d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
+                      row0 + x * kTM, hh, bb);
       int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
       bool ok = true;
       int next_ent = col_idx[e0];
@@ -169,8 +171,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
           mbar_expect_tx(bar(L::kKVFull + s), L::kTile);
           for (int r = 0; r < kBoxes; ++r)
-            tma_load_3d(sb + L::KV + s * L::kTile + r * 16384u, part == 0 ? &tmk : &tmv,
-                        bar(L::kKVFull + s), 64 * r, kt * kTN, bh);
+            tma_load_4d(sb + L::KV + s * L::kTile + r * 16384u, part == 0 ? &tmk : &tmv,
+                        bar(L::kKVFull + s), 64 * r, kt * kTN, hh, bb);
           issued = e + 1;
         }
       }
@@ -378,7 +380,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       named_bar_sync(1 + x, 128);
       if (r == 0) {
         for (int b = 0; b < kBoxes; ++b)
-          tma_store_3d(&tmo, stage + (uint32_t)b * 16384u, 64 * b, row0 + x * kTM, bh);
+          tma_store_4d(&tmo, stage + (uint32_t)b * 16384u, 64 * b, row0 + x * kTM, hh, bb);
         bulk_commit();
         bulk_wait_read0();
       }
@@ -413,14 +415,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 template <typename T, int D, int STAGES>
 int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse, int BH,
-                  float scale, const MaskParams& mp, const int32_t* rp, const int32_t* ci,
-                  int* status, cudaStream_t s) {
+                  float scale, const MaskParams& mp, const Views& vw, const int32_t* rp,
+                  const int32_t* ci, int* status, cudaStream_t s) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mo;
-  if (int rc = tc::make_tmap_3d(&mq, q, kBF16, D, (uint64_t)mp.n_q, (uint64_t)BH, kTM)) return rc;
-  if (int rc = tc::make_tmap_3d(&mk, k, kBF16, D, (uint64_t)mp.n_kv, (uint64_t)BH, kTN)) return rc;
-  if (int rc = tc::make_tmap_3d(&mv, v, kBF16, D, (uint64_t)mp.n_kv, (uint64_t)BH, kTN)) return rc;
-  if (int rc = tc::make_tmap_3d(&mo, o, kBF16, D, (uint64_t)mp.n_q, (uint64_t)BH, kTM)) return rc;
+  const uint64_t nh = (uint64_t)vw.heads, nb = (uint64_t)(BH / vw.heads);
+  if (int rc = tc::make_tmap_4d(&mq, q, kBF16, D, (uint64_t)mp.n_q, nh, nb, vw.q, kTM)) return rc;
+  if (int rc = tc::make_tmap_4d(&mk, k, kBF16, D, (uint64_t)mp.n_kv, nh, nb, vw.k, kTN)) return rc;
+  if (int rc = tc::make_tmap_4d(&mv, v, kBF16, D, (uint64_t)mp.n_kv, nh, nb, vw.v, kTN)) return rc;
+  if (int rc = tc::make_tmap_4d(&mo, o, kBF16, D, (uint64_t)mp.n_q, nh, nb, vw.o, kTM)) return rc;
   using L = FwdLayout<D, STAGES>;
   auto kern = fwd_tc_kernel<T, D, STAGES>;
   if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -431,7 +434,7 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
   {
     LaunchScope ls("fwd_tc_kernel", s);
     kern<<<grid, kFwdThreads, L::kAlloc, s>>>(mq, mk, mv, mo, (T*)o, lse, scale * kLog2e, mp, rp,
-                                             ci, status);
+                                             ci, vw.heads, vw.o, status);
   }
   return check_launch("fwd_tc_kernel");
 }
@@ -439,17 +442,24 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
 }  // namespace
 
 namespace tc {
-int make_tmap_3d(CUtensorMap* map, const void* base, bool bf16, uint64_t cols, uint64_t rows,
-                 uint64_t planes, uint32_t box_rows) {
+bool tma_compatible(const void* base, const Strides3& st) {
+  return ((uintptr_t)base & 15u) == 0 && st.b % 8 == 0 && st.h % 8 == 0 && st.n % 8 == 0 &&
+         st.b > 0 && st.h > 0 && st.n > 0;
+}
+
+int make_tmap_4d(CUtensorMap* map, const void* base, bool bf16, uint64_t cols, uint64_t rows,
+                 uint64_t heads, uint64_t batch, const Strides3& st, uint32_t box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(SBFA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  if (((uintptr_t)base & 15u) != 0)
-    return fail(SBFA_ERR_INVALID, "tensor-core path: tensors must be 16-byte aligned");
-  cuuint64_t dims[3] = {cols, rows, planes};
-  cuuint64_t strides[2] = {cols * 2, cols * rows * 2};
-  cuuint32_t box[3] = {64, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+  if (!tma_compatible(base, st))
+    return fail(SBFA_ERR_INVALID,
+                "tensor-core path: tensors must be 16-byte aligned with batch, head and row "
+                "strides that are positive multiples of 8 elements");
+  cuuint64_t dims[4] = {cols, rows, heads, batch};
+  cuuint64_t strides[3] = {(cuuint64_t)st.n * 2, (cuuint64_t)st.h * 2, (cuuint64_t)st.b * 2};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -472,15 +482,17 @@ int tc_tiles(int pass, int64_t* tm, int64_t* tn) {
 }
 
 int tc_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o, float* lse,
-           int BH, float scale, const MaskParams& mp, const int32_t* rp, const int32_t* ci,
-           int* status, cudaStream_t s) {
+           int BH, float scale, const MaskParams& mp, const Views& vw, const int32_t* rp,
+           const int32_t* ci, int* status, cudaStream_t s) {
   const bool bf = dtype == SBFA_BF16;
   if (D == 128)
-    return bf ? launch_fwd_tc<__nv_bfloat16, 128, 5>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
-              : launch_fwd_tc<__half, 128, 5>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
+    return bf ? launch_fwd_tc<__nv_bfloat16, 128, 5>(q, k, v, o, lse, BH, scale, mp, vw, rp, ci,
+                                                     status, s)
+              : launch_fwd_tc<__half, 128, 5>(q, k, v, o, lse, BH, scale, mp, vw, rp, ci, status, s);
   if (D == 64)
-    return bf ? launch_fwd_tc<__nv_bfloat16, 64, 8>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s)
-              : launch_fwd_tc<__half, 64, 8>(q, k, v, o, lse, BH, scale, mp, rp, ci, status, s);
+    return bf ? launch_fwd_tc<__nv_bfloat16, 64, 8>(q, k, v, o, lse, BH, scale, mp, vw, rp, ci,
+                                                    status, s)
+              : launch_fwd_tc<__half, 64, 8>(q, k, v, o, lse, BH, scale, mp, vw, rp, ci, status, s);
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core forward: head_dim must be 64 or 128");
 }
 

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                    T* __restrict__ dv, const float* __restrict__ lse,
                    const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
                    const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
-                   int n_tj, int* status) {
+                   int n_tj, int heads, Strides3 sdk, Strides3 sdv, int* status) {
   using L = DkdvLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bh = idx / (n_tj - 1);
     tj = 1 + idx % (n_tj - 1);
   }
+  const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
   const int e0 = col_ptr[tj];
   const int nq = col_ptr[tj + 1] - e0;
 
@@ -148,9 +149,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int rr = idx / (D / 8), cc = idx % (D / 8);
       const int key = tj * kT + rr;
       if (key < mp.n_kv) {
-        const size_t off = ((size_t)bh * mp.n_kv + key) * D;
-        reinterpret_cast<uint4*>(dk + off)[cc] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(dv + off)[cc] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dk + bb * sdk.b + hh * sdk.h + (int64_t)key * sdk.n)[cc] =
+            make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dv + bb * sdv.b + hh * sdv.h + (int64_t)key * sdv.n)[cc] =
+            make_uint4(0, 0, 0, 0);
       }
     }
     return;
@@ -191,8 +193,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (lane == 0) {
         mbar_expect_tx(bar(L::kKVFull), 2 * L::kTile);
         for (int r = 0; r < kBoxes; ++r) {
-          tma_load_3d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, bh);
-          tma_load_3d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, bh);
+          tma_load_4d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
+          tma_load_4d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
         }
       }
       int issued = 0;
@@ -211,8 +213,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (lane == 0) {
             mbar_expect_tx(bar(L::kRFull + s), L::kTile);
             for (int r = 0; r < kBoxes; ++r)
-              tma_load_3d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmdo : &tmq,
-                          bar(L::kRFull + s), 64 * r, ti * kT, bh);
+              tma_load_4d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmdo : &tmq,
+                          bar(L::kRFull + s), 64 * r, ti * kT, hh, bb);
           }
           issued = e + 1;
         }
@@ -445,8 +447,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       named_bar_sync(1 + grp, 128);
       if (r == 0) {
         for (int b = 0; b < kBoxes; ++b)
-          tma_store_3d(grp == 0 ? &tmdv : &tmdk, stage + (uint32_t)b * 16384u, 64 * b, tj * kT,
-                       bh);
+          tma_store_4d(grp == 0 ? &tmdv : &tmdk, stage + (uint32_t)b * 16384u, 64 * b, tj * kT,
+                       hh, bb);
         bulk_commit();
         bulk_wait_read0();
       }
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  const __grid_constant__ CUtensorMap tmdq, T* __restrict__ dq,
                  const float* __restrict__ lse, const float* __restrict__ delta, float scale,
                  float scale_log2, MaskParams mp, const int32_t* __restrict__ row_ptr,
-                 const int32_t* __restrict__ col_idx, int* status) {
+                 const int32_t* __restrict__ col_idx, int heads, Strides3 sdq, int* status) {
   using L = DqLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 q, N=128 keys
@@ -518,6 +520,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ti = blockIdx.x;
   const int bh = blockIdx.y;
+  const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
   const int e0 = row_ptr[ti];
   const int nk = row_ptr[ti + 1] - e0;
 
@@ -526,7 +529,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int rr = idx / (D / 8), cc = idx % (D / 8);
       const int row = ti * kT + rr;
       if (row < mp.n_q)
-        reinterpret_cast<uint4*>(dq + ((size_t)bh * mp.n_q + row) * D)[cc] =
+        reinterpret_cast<uint4*>(dq + bb * sdq.b + hh * sdq.h + (int64_t)row * sdq.n)[cc] =
             make_uint4(0, 0, 0, 0);
     }
     return;
@@ -563,8 +566,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // ---------------------------------------------------------- producer
       mbar_expect_tx(bar(L::kQFull), 2 * L::kTile);
       for (int r = 0; r < kBoxes; ++r) {
-        tma_load_3d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, bh);
-        tma_load_3d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, bh);
+        tma_load_4d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
+        tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
       }
       int issued = 0;
       int next_ent = col_idx[e0];
@@ -581,8 +584,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           mbar_expect_tx(bar(L::kRFull + s), L::kTile);
           for (int r = 0; r < kBoxes; ++r)
-            tma_load_3d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmk : &tmv,
-                        bar(L::kRFull + s), 64 * r, kt * kT, bh);
+            tma_load_4d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmk : &tmv,
+                        bar(L::kRFull + s), 64 * r, kt * kT, hh, bb);
           issued = e + 1;
         }
       }
@@ -753,7 +756,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       named_bar_sync(1 + grp, 128);
       if (r == 0) {
-        tma_store_3d(&tmdq, region, 64 * grp, ti * kT, bh);
+        tma_store_4d(&tmdq, region, 64 * grp, ti * kT, hh, bb);
         bulk_commit();
         bulk_wait_read0();
       }
@@ -771,18 +774,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 template <typename T, int D>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
-                  const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
-                  const int32_t* kv_cp, const int32_t* kv_ri, int* status, cudaStream_t s) {
+                  const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
+                  const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
+                  cudaStream_t s) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
-  const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv, bh = (uint64_t)BH;
-  if (int rc = make_tmap_3d(&mq, q, kBF16, D, nq, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mdo, dout, kBF16, D, nq, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mk, k, kBF16, D, nkv, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mv, v, kBF16, D, nkv, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mdq, dq, kBF16, D, nq, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mdk, dk, kBF16, D, nkv, bh, kT)) return rc;
-  if (int rc = make_tmap_3d(&mdv, dv, kBF16, D, nkv, bh, kT)) return rc;
+  const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv;
+  const uint64_t nh = (uint64_t)vw.heads, nb = (uint64_t)(BH / vw.heads);
+  if (int rc = make_tmap_4d(&mq, q, kBF16, D, nq, nh, nb, vw.q, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdo, dout, kBF16, D, nq, nh, nb, vw.dout, kT)) return rc;
+  if (int rc = make_tmap_4d(&mk, k, kBF16, D, nkv, nh, nb, vw.k, kT)) return rc;
+  if (int rc = make_tmap_4d(&mv, v, kBF16, D, nkv, nh, nb, vw.v, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdq, dq, kBF16, D, nq, nh, nb, vw.dq, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdk, dk, kBF16, D, nkv, nh, nb, vw.dk, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdv, dv, kBF16, D, nkv, nh, nb, vw.dv, kT)) return rc;
   const float sl = scale * kLog2e;
   {
     using L = DkdvLayout<D>;
@@ -795,7 +800,7 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     LaunchScope ls("dkdv_tc_kernel", s);
     kern<<<n_tj * BH, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse,
                                                   delta, scale, sl, mp, kv_cp, kv_ri, BH, n_tj,
-                                                  status);
+                                                  vw.heads, vw.dk, vw.dv, status);
   }
   if (int rc = check_launch("dkdv_tc_kernel")) return rc;
   {
@@ -808,34 +813,33 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     dim3 grid(ceil_div_i(mp.n_q, kT), BH);
     LaunchScope ls("dq_tc_kernel", s);
     kern<<<grid, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdq, (T*)dq, lse, delta, scale, sl,
-                                              mp, dq_rp, dq_ci, status);
+                                              mp, dq_rp, dq_ci, vw.heads, vw.dq, status);
   }
   return check_launch("dq_tc_kernel");
 }
 
 }  // namespace
 
-int generic_delta(int dtype, const void* o, const void* dout, float* delta, int64_t rows, int D,
-                  cudaStream_t s);
+int generic_delta(int dtype, const void* o, const void* dout, float* delta, int BH, int n_q,
+                  int D, const Views& vw, cudaStream_t s);
 
 int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta, int BH,
-           float scale, const MaskParams& mp, const int32_t* dq_rp, const int32_t* dq_ci,
-           const int32_t* kv_cp, const int32_t* kv_ri, int* status, cudaStream_t s) {
-  if (int rc = generic_delta(dtype, o, dout, delta, (int64_t)BH * mp.n_q, D, s)) return rc;
+           float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
+           const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
+           cudaStream_t s) {
+  if (int rc = generic_delta(dtype, o, dout, delta, BH, mp.n_q, D, vw, s)) return rc;
   const bool bf = dtype == SBFA_BF16;
   if (D == 128)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
-                                                        scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
-                                                        status, s)
-              : launch_bwd_tc<__half, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
-                                                 mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
+    return bf ? launch_bwd_tc<__nv_bfloat16, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+                                                  mp, vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s)
+              : launch_bwd_tc<__half, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp,
+                                           vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   if (D == 64)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH,
-                                                       scale, mp, dq_rp, dq_ci, kv_cp, kv_ri,
-                                                       status, s)
-              : launch_bwd_tc<__half, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
-                                                mp, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
+    return bf ? launch_bwd_tc<__nv_bfloat16, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
+                                                 mp, vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s)
+              : launch_bwd_tc<__half, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw,
+                                          dq_rp, dq_ci, kv_cp, kv_ri, status, s);
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward: head_dim must be 64 or 128");
 }
 

@@ -18,12 +18,12 @@ namespace sbfa {
 int generic_tiles(int pass, int64_t* tm, int64_t* tn);
 bool generic_supports(int dtype, int64_t D);
 int generic_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o,
-                float* lse, int BH, double scale, const MaskParams& mp, const int32_t* rp,
-                const int32_t* ci, cudaStream_t s);
+                float* lse, int BH, double scale, const MaskParams& mp, const Views& vw,
+                const int32_t* rp, const int32_t* ci, cudaStream_t s);
 int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                int BH, double scale, const MaskParams& mp, const int32_t* a, const int32_t* b,
-                const int32_t* c, const int32_t* d, cudaStream_t s);
+                int BH, double scale, const MaskParams& mp, const Views& vw, const int32_t* a,
+                const int32_t* b, const int32_t* c, const int32_t* d, cudaStream_t s);
 // decode.cu
 int decode_tile();
 int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t window);
@@ -37,13 +37,16 @@ int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, 
 bool tc_supports(int pass, int dtype, int64_t D);
 int tc_tiles(int pass, int64_t* tm, int64_t* tn);
 int tc_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* o, float* lse,
-           int BH, float scale, const MaskParams& mp, const int32_t* rp, const int32_t* ci,
-           int* status, cudaStream_t s);
+           int BH, float scale, const MaskParams& mp, const Views& vw, const int32_t* rp,
+           const int32_t* ci, int* status, cudaStream_t s);
 int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-           int BH, float scale, const MaskParams& mp, const int32_t* dq_rp,
+           int BH, float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
            const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
            cudaStream_t s);
+namespace tc {
+bool tma_compatible(const void* base, const Strides3& st);
+}
 
 namespace {
 thread_local std::string g_last_error;
@@ -158,12 +161,46 @@ MaskParams make_mp(int64_t n_q, int64_t n_kv, int is_causal, int64_t sink, int64
 
 bool use_tc(int pass, int dtype, int64_t D) { return tc_supports(pass, dtype, D); }
 
+// Views of a call: strides == NULL means every tensor is contiguous
+// [B, H, N, D]; otherwise strides holds (batch, head, row) element strides for
+// each of the `count` tensors in the order of Views' members.
+int make_views(const int64_t* strides, int count, int64_t H, int64_t n_q, int64_t n_kv,
+               int64_t D, Views* vw) {
+  Strides3* dst[8] = {&vw->q, &vw->k, &vw->v, &vw->o, &vw->dout, &vw->dq, &vw->dk, &vw->dv};
+  const bool kv_rows[8] = {false, true, true, false, false, false, true, true};
+  vw->heads = (int)H;
+  for (int t = 0; t < 8; ++t) {
+    const int64_t n = kv_rows[t] ? n_kv : n_q;
+    if (strides == nullptr || t >= count) {
+      *dst[t] = Strides3{H * n * D, n * D, D};
+    } else {
+      const int64_t* st = strides + 3 * t;
+      if (st[0] < 0 || st[1] < 0 || st[2] < D)
+        return fail(SBFA_ERR_INVALID,
+                    "strides must be non-negative and rows at least head_dim apart");
+      *dst[t] = Strides3{st[0], st[1], st[2]};
+    }
+  }
+  return SBFA_OK;
+}
+
+// The tensor-core kernels read every tensor through TMA maps.
+int check_tma(const void* const* ptrs, const Strides3* const* st, int count, const char* who) {
+  for (int t = 0; t < count; ++t)
+    if (!tc::tma_compatible(ptrs[t], *st[t]))
+      return fail(SBFA_ERR_INVALID,
+                  std::string(who) + ": for float16/bfloat16 with head_dim 64 or 128 every "
+                  "tensor must be 16-byte aligned with batch, head and row strides that are "
+                  "positive multiples of 8 elements");
+  return SBFA_OK;
+}
+
 }  // namespace
 }  // namespace sbfa
 
 using namespace sbfa;
 
-extern "C" int sbfa_abi_version(void) { return 1; }
+extern "C" int sbfa_abi_version(void) { return 2; }
 
 extern "C" int64_t sbfa_launch_count(void) { return g_launches.load(); }
 
@@ -259,21 +296,27 @@ extern "C" int sbfa_fwd(const void* q, const void* k, const void* v, void* o, fl
                         int dtype, double softmax_scale, int is_causal, int64_t sink,
                         int64_t window, const int32_t* block_mask, int64_t block_m,
                         int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
-                        void* stream) {
+                        const int64_t* strides, void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
   if (!q || !k || !v || !o || !lse || !row_ptr || !col_idx)
     return fail(SBFA_ERR_INVALID, "sbfa_fwd: NULL tensor or plan pointer");
+  Views vw;
+  if (int rc = make_views(strides, 4, H, n_q, n_kv, head_dim, &vw)) return rc;
   MaskParams mp = make_mp(n_q, n_kv, is_causal, sink, window, block_mask, block_m, block_n);
   cudaStream_t s = (cudaStream_t)stream;
   const int BH = (int)(B * H);
-  if (use_tc(0, dtype, head_dim))
-    return tc_fwd(dtype, (int)head_dim, q, k, v, o, lse, BH, softmax_scale, mp, row_ptr,
+  if (use_tc(0, dtype, head_dim)) {
+    const void* ptrs[4] = {q, k, v, o};
+    const Strides3* st[4] = {&vw.q, &vw.k, &vw.v, &vw.o};
+    if (int rc = check_tma(ptrs, st, 4, "sbfa_fwd")) return rc;
+    return tc_fwd(dtype, (int)head_dim, q, k, v, o, lse, BH, softmax_scale, mp, vw, row_ptr,
                   col_idx, device_status_ptr(), s);
+  }
   if (!generic_supports(dtype, head_dim))
     return fail(SBFA_ERR_UNSUPPORTED, "head_dim too large (max 256; 128 for float64)");
-  return generic_fwd(dtype, (int)head_dim, q, k, v, o, lse, BH, softmax_scale, mp, row_ptr,
+  return generic_fwd(dtype, (int)head_dim, q, k, v, o, lse, BH, softmax_scale, mp, vw, row_ptr,
                      col_idx, s);
 }
 
@@ -284,7 +327,7 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
                         int64_t sink, int64_t window, const int32_t* block_mask,
                         int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
                         const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
-                        const int32_t* kv_row_idx, void* stream) {
+                        const int32_t* kv_row_idx, const int64_t* strides, void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
@@ -292,17 +335,23 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
     return fail(SBFA_ERR_INVALID, "sbfa_bwd: NULL tensor pointer");
   if (!dq_row_ptr || !dq_col_idx || !kv_col_ptr || !kv_row_idx)
     return fail(SBFA_ERR_INVALID, "sbfa_bwd: NULL plan pointer");
+  Views vw;
+  if (int rc = make_views(strides, 8, H, n_q, n_kv, head_dim, &vw)) return rc;
   MaskParams mp = make_mp(n_q, n_kv, is_causal, sink, window, block_mask, block_m, block_n);
   cudaStream_t s = (cudaStream_t)stream;
   const int BH = (int)(B * H);
-  if (use_tc(1, dtype, head_dim))
+  if (use_tc(1, dtype, head_dim)) {
+    const void* ptrs[7] = {q, k, v, dout, dq, dk, dv};
+    const Strides3* st[7] = {&vw.q, &vw.k, &vw.v, &vw.dout, &vw.dq, &vw.dk, &vw.dv};
+    if (int rc = check_tma(ptrs, st, 7, "sbfa_bwd")) return rc;
     return tc_bwd(dtype, (int)head_dim, q, k, v, o, lse, dout, dq, dk, dv, delta_ws, BH,
-                  softmax_scale, mp, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx,
+                  softmax_scale, mp, vw, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx,
                   device_status_ptr(), s);
+  }
   if (!generic_supports(dtype, head_dim))
     return fail(SBFA_ERR_UNSUPPORTED, "head_dim too large (max 256; 128 for float64)");
   return generic_bwd(dtype, (int)head_dim, q, k, v, o, lse, dout, dq, dk, dv, delta_ws, BH,
-                     softmax_scale, mp, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx, s);
+                     softmax_scale, mp, vw, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx, s);
 }
 
 

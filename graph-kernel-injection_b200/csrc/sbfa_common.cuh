@@ -65,6 +65,23 @@ struct MaskParams {
   int causal;
 };
 
+// Element strides (batch, head, row) of one [B, H, N, D] tensor whose last
+// dimension is unit-stride (upstream makes every input contiguous first,
+// sparse_triton_kernel.py:834; here views are read in place).
+struct Strides3 {
+  int64_t b, h, n;
+};
+
+// Strides of every tensor of a call and the head count that splits the
+// flattened (batch, head) index bh into (bh / heads, bh % heads).
+struct Views {
+  Strides3 q, k, v, o, dout, dq, dk, dv;
+  int heads;
+  __host__ __device__ __forceinline__ int64_t at(const Strides3& s, int bh, int64_t row) const {
+    return (int64_t)(bh / heads) * s.b + (int64_t)(bh % heads) * s.h + row * s.n;
+  }
+};
+
 // Token rule of sparse_triton_kernel.py:315-319 at absolute positions.
 __device__ __forceinline__ bool token_visible(int qpos, int k, int sink, int window) {
   return (k <= qpos) && (k < sink || k >= qpos - window + 1);

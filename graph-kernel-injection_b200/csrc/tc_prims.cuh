@@ -87,6 +87,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // TMA tiled store shared -> global (no reduction); completion tracked with
 // the bulk async-group of the issuing thread.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y,
@@ -95,6 +104,14 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
       "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {
@@ -337,10 +354,15 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
 // ---------------------------------------------------------------------------
 // Host: tensor maps
 // ---------------------------------------------------------------------------
-// 3-D map over a contiguous [planes][rows][cols] 16-bit tensor with a
-// {64, box_rows, 1} box and the 128-byte swizzle (OOB rows read as zero).
-int make_tmap_3d(CUtensorMap* map, const void* base, bool bf16, uint64_t cols, uint64_t rows,
-                 uint64_t planes, uint32_t box_rows);
+// 4-D map over a [B][H][rows][cols] 16-bit tensor with element strides
+// st (batch, head, row; unit-stride cols), a {64, box_rows, 1, 1} box and the
+// 128-byte swizzle (OOB rows read as zero, OOB stores are clipped).  Tiles
+// never cross a (batch, head) boundary.  The base must be 16-byte aligned and
+// every stride a multiple of 8 elements.
+int make_tmap_4d(CUtensorMap* map, const void* base, bool bf16, uint64_t cols, uint64_t rows,
+                 uint64_t heads, uint64_t batch, const Strides3& st, uint32_t box_rows);
+// True when (base, strides) satisfy the TMA rules above for 16-bit elements.
+bool tma_compatible(const void* base, const Strides3& st);
 
 }  // namespace tc
 }  // namespace sbfa

@@ -28,10 +28,11 @@ visible key give ``O = 0`` and zero gradients.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import weakref
 from dataclasses import dataclass
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -218,6 +219,51 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_mask: tor
     return B, H, N_Q, N_KV, D
 
 
+_TC_DTYPES = (torch.float16, torch.bfloat16)
+
+
+def _strides3(t: torch.Tensor) -> List[int]:
+    """(batch, head, row) element strides of a [B, H, N, D] tensor whose last
+    dimension is unit-stride; a size-1 dimension gets the extent of the
+    dimensions inside it (any stride is valid there, and this one also
+    satisfies the tensor-core alignment rules whenever the others do)."""
+    shape, st = t.shape, list(t.stride())
+    out = []
+    for i in range(3):
+        if shape[i] == 1:
+            out.append(max(st[j] * shape[j] for j in range(i + 1, 4)))
+        else:
+            out.append(st[i])
+    return out
+
+
+def _readable(t: torch.Tensor, tensor_core: bool) -> torch.Tensor:
+    """``t`` itself when the kernels can read it in place, else a contiguous
+    copy (upstream always copies: ``sparse_triton_kernel.py:707, 834``).
+    Reads may overlap (an expanded dimension is fine for the CUDA-core
+    kernels); the tensor-core kernels read through TMA, which needs a 16-byte
+    aligned base and strides that are positive multiples of 8 elements."""
+    if t.stride(-1) != 1 and t.shape[-1] != 1:
+        return t.contiguous()
+    if t.is_contiguous():
+        return t
+    st = _strides3(t)
+    if st[2] < t.shape[-1] or min(st) < 0:
+        return t.contiguous()
+    if tensor_core and (t.data_ptr() % 16 or any(x <= 0 or x % 8 for x in st)):
+        return t.contiguous()
+    return t
+
+
+def _uses_tensor_cores(dtype: torch.dtype, d: int) -> bool:
+    return dtype in _TC_DTYPES and d in (64, 128)
+
+
+def _stride_array(*ts: torch.Tensor):
+    vals = [x for t in ts for x in _strides3(t)]
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
 class _BlockSparseFlashAttention(torch.autograd.Function):
     """Autograd bridge to the libsbfa forward / decode / backward kernels
     (upstream ``sparse_triton_kernel.py:609-779``)."""
@@ -231,14 +277,19 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
         native.dtype_code(q.dtype)
         dev = q.device
         block_mask = block_mask.to(device=dev, dtype=torch.int32).contiguous()
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        o = torch.empty_like(q)
-        lse = torch.empty((B, H, N_Q), dtype=torch.float32, device=dev)
         code = native.dtype_code(q.dtype)
         L = native.lib()
+        decode = N_Q == 1 and bool(L.sbfa_decode_supported(code, D))
+        if decode:  # the decode kernel reads contiguous q / k / v
+            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        else:       # strided views are read in place
+            tcore = _uses_tensor_cores(q.dtype, D)
+            q, k, v = (_readable(t, tcore) for t in (q, k, v))
+        o = torch.empty((B, H, N_Q, D), dtype=q.dtype, device=dev)
+        lse = torch.empty((B, H, N_Q), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
             stream = native.stream_ptr(dev)
-            if N_Q == 1 and L.sbfa_decode_supported(code, D):
+            if decode:
                 plan = _plan_for(block_mask, 3, q.dtype, D, N_Q, N_KV, block_m, block_n)
                 ws_bytes = int(L.sbfa_decode_workspace_bytes(B, H, N_KV, D, block_n))
                 ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
@@ -254,7 +305,8 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                     q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                     B, H, N_Q, N_KV, D, code, float(softmax_scale), int(bool(is_causal)),
                     int(sink_size), int(window_size), block_mask.data_ptr(), block_m, block_n,
-                    plan["row_ptr"].data_ptr(), plan["col_idx"].data_ptr(), stream), "fwd")
+                    plan["row_ptr"].data_ptr(), plan["col_idx"].data_ptr(),
+                    _stride_array(q, k, v, o), stream), "fwd")
         ctx.save_for_backward(q, k, v, o, lse, block_mask)
         ctx.softmax_scale = float(softmax_scale)
         ctx.block_m = int(block_m)
@@ -268,15 +320,16 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do: torch.Tensor) -> Tuple[Optional[torch.Tensor], ...]:
         q, k, v, o, lse, block_mask = ctx.saved_tensors
-        do = do.contiguous()
         if do.dtype != q.dtype:
             do = do.to(q.dtype)
         B, H, N_Q, D = q.shape
         N_KV = k.shape[2]
         dev = q.device
-        dq = torch.empty_like(q)
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
+        tcore = _uses_tensor_cores(q.dtype, D)
+        do = _readable(do, tcore)
+        # gradients in the layout of their inputs, so they flow back through
+        # the caller's transposes without a copy
+        dq, dk, dv = (_readable(torch.empty_like(t), tcore) for t in (q, k, v))
         delta = torch.empty((B, H, N_Q), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
             p_dq = _plan_for(block_mask, 1, q.dtype, D, N_Q, N_KV, ctx.block_m, ctx.block_n)
@@ -288,7 +341,8 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                 int(ctx.is_causal), ctx.sink_size, ctx.window_size, block_mask.data_ptr(),
                 ctx.block_m, ctx.block_n, p_dq["row_ptr"].data_ptr(),
                 p_dq["col_idx"].data_ptr(), p_kv["col_ptr"].data_ptr(),
-                p_kv["row_idx"].data_ptr(), native.stream_ptr(dev)), "bwd")
+                p_kv["row_idx"].data_ptr(), _stride_array(q, k, v, o, do, dq, dk, dv),
+                native.stream_ptr(dev)), "bwd")
         return dq, dk, dv, None, None, None, None, None, None, None
 
 
@@ -308,8 +362,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(q.shape[-1])
     return _BlockSparseFlashAttention.apply(
-        q.contiguous(), k.contiguous(), v.contiguous(), block_mask, float(softmax_scale),
-        int(block_m), int(block_n), bool(is_causal), int(sink_size), int(window_size))
+        q, k, v, block_mask, float(softmax_scale), int(block_m), int(block_n), bool(is_causal),
+        int(sink_size), int(window_size))
 
 
 # ---------------------------------------------------------------------------

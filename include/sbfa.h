@@ -120,6 +120,18 @@ int sbfa_plan_tiles(int pass, int dtype, int64_t head_dim, int64_t n_q,
 /* Common shape/semantic arguments, in this order, for the calls below:
  *   B, H, n_q, n_kv, head_dim, dtype, softmax_scale, is_causal, sink, window,
  *   block_mask, block_m, block_n
+ *
+ * Tensor layout: logical [B, H, N, head_dim] with a unit-stride last
+ * dimension.  strides == NULL means every tensor is contiguous; otherwise it
+ * points to host int64 element strides (batch, head, row) for each tensor,
+ * three per tensor, in the order the call lists (sbfa_fwd: q, k, v, o;
+ * sbfa_bwd: q, k, v, o, dout, dq, dk, dv), so transposed views such as the
+ * [B, N, H, D] memory behind Llama-style attention are read in place (upstream
+ * copies them with .contiguous(), sparse_triton_kernel.py:707, 834).  For
+ * float16/bfloat16 with head_dim 64 or 128 (the tensor-core kernels, which read
+ * through TMA) every tensor must be 16-byte aligned and its strides positive
+ * multiples of 8 elements, else SBFA_ERR_INVALID.  lse and delta_ws are always
+ * contiguous [B, H, n_q].
  */
 
 /* Forward: O = softmax(Q K^T * scale  masked) V, LSE = natural-log
@@ -132,7 +144,7 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
              int dtype, double softmax_scale, int is_causal, int64_t sink,
              int64_t window, const int32_t* block_mask, int64_t block_m,
              int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
-             void* stream);
+             const int64_t* strides, void* stream);
 
 /* Backward: dQ, dK, dV (written, not accumulated) from Q, K, V, O, dO and
  * the forward's LSE.  Replaces _bwd_preprocess_kernel, _bwd_dkdv_kernel,
@@ -147,7 +159,7 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              int64_t sink, int64_t window, const int32_t* block_mask,
              int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
              const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
-             const int32_t* kv_row_idx, void* stream);
+             const int32_t* kv_row_idx, const int64_t* strides, void* stream);
 
 /* Split-KV decode for n_q == 1 (the upstream path is _fwd_kernel with
  * N_Q = 1, BLOCK_M = 1: benchmark.py:799-804 -> sparse_triton_kernel.py:231).

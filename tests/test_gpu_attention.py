@@ -284,3 +284,51 @@ def test_tensor_core_path_empty_rows(dtype, D):
         for a, b, kind in ((o, ro, "fwd"), (dq, rdq, "bwd"), (dk, rdk, "bwd"), (dv, rdv, "bwd")):
             close(a, b, dtype, kind)
     assert native.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64),
+                                     (torch.float32, 64), (torch.bfloat16, 96)])
+def test_strided_views_read_in_place(dtype, D):
+    """Q/K/V as transposes of [B, N, H, D] storage (the layout behind
+    Llama-style attention) and dO as a transposed view: the kernels read them
+    through their strides, with results bit-identical to the contiguous call
+    (same data, same arithmetic) and equal to the oracle."""
+    B, H, n, S, W, bm = 2, 3, 640, 4, 192, 64
+    g = torch.Generator(device=DEV).manual_seed(5)
+    base = [torch.randn(B, n, H, D, generator=g, device=DEV, dtype=dtype) for _ in range(4)]
+    q, k, v, do = (t.transpose(1, 2) for t in base)
+    assert not q.is_contiguous()
+    mask = stk.make_streaming_mask(n, n, stk.StreamingMaskSpec(S, W), bm, bm, DEV)
+    outs = []
+    for qq, kk, vv, gg in ((q, k, v, do), tuple(t.contiguous() for t in (q, k, v, do))):
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (qq, kk, vv))
+        o = stk.block_sparse_attention(qq, kk, vv, mask, block_m=bm, block_n=bm, is_causal=True,
+                                       sink_size=S, window_size=W)
+        o.backward(gg)
+        outs.append((o.detach(), qq.grad, kk.grad, vv.grad))
+    assert native.device_status() == 0
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    ro, rdq, rdk, rdv = orc.attention_forward_backward(
+        q.double().cpu(), k.double().cpu(), v.double().cpu(), do.double().cpu(), mask.cpu(),
+        block_m=bm, block_n=bm, is_causal=True, sink_size=S, window_size=W)
+    close(outs[0][0], ro, dtype, "fwd")
+    for got, ref in zip(outs[0][1:], (rdq, rdk, rdv)):
+        close(got, ref, dtype, "bwd")
+
+
+def test_unaligned_view_falls_back_to_copy():
+    """A view whose row stride is not a multiple of 8 elements cannot be read
+    by TMA; the bridge copies it (as upstream always does) and the result is
+    unchanged."""
+    B, H, n, D = 1, 2, 256, 64
+    g = torch.Generator(device=DEV).manual_seed(6)
+    wide = torch.randn(B, H, n, D + 4, generator=g, device=DEV, dtype=torch.bfloat16)
+    q = wide[..., :D]  # row stride D + 4
+    k, v = (torch.randn(B, H, n, D, generator=g, device=DEV, dtype=torch.bfloat16)
+            for _ in range(2))
+    mask = stk.make_streaming_mask(n, n, stk.StreamingMaskSpec(4, 64), 64, 64, DEV)
+    kw = dict(block_m=64, block_n=64, is_causal=True, sink_size=4, window_size=64)
+    a = stk.block_sparse_attention(q, k, v, mask, **kw)
+    b = stk.block_sparse_attention(q.contiguous(), k, v, mask, **kw)
+    assert torch.equal(a, b)
