@@ -365,10 +365,30 @@ def bench_decode(dist, args, pk, src):
     ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
     value = kv_bytes * dist.world * steps / (ms / 1e3) / 1e9
     rl = roofline(per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes, workload="cfg4")
-    del q, k, v
+
+    # the same decode over a StreamingLLM ring cache holding sink + window rows
+    from streaming_kv_cache import StreamingKVCache
+    cache = StreamingKVCache(cfg["B"], cfg["H"], cfg["D"], cfg["S"], cfg["W"], dtype=cfg["dtype"])
+    cache.append(k, v)
+    full_bytes = 2 * k.numel() * k.element_size()
+    del k, v
+    torch.cuda.empty_cache()
+
+    def ring_step():
+        return cache.attend(q)
+
+    r_ms, r_launches, r_per_kernel = time_steps(dist, ring_step, steps, args.warmup)
+    ring = {"value": round(kv_bytes * dist.world * steps / (r_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(r_ms / steps, 4), "cache_bytes": cache.memory_bytes,
+            "full_cache_bytes": full_bytes,
+            "memory_ratio": round(full_bytes / cache.memory_bytes, 2),
+            "roofline": roofline(r_per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes,
+                                 workload="cfg4_ring"),
+            "gpu_launches": r_launches}
+    del q, cache
     torch.cuda.empty_cache()
     return dict(value=value, ms=ms / steps, roofline=rl, kv_bytes=kv_bytes, qo_bytes=qo_bytes,
-                launches=launches)
+                launches=launches, ring=ring)
 
 
 def bench_fx(dist, args, pk, src):
@@ -562,6 +582,7 @@ def main():
                                 "ms_per_step": round(r["ms"], 4), "roofline": r["roofline"],
                                 "kv_bytes_per_step": r["kv_bytes"],
                                 "gpu_launches": r["launches"]}
+        extra["cfg4_decode_ring_cache"] = r["ring"]
         if args.workload == "decode":
             line.update({"metric": "decode KV GB/s", "unit": "GB/s", "value": extra[
                 "cfg4_decode"]["value"], "roofline": r["roofline"], "dtype": "fp16"})

@@ -22,6 +22,9 @@
 #include "sbfa_common.cuh"
 
 namespace sbfa {
+
+int decode_group(int dtype, int64_t D);
+
 namespace {
 
 constexpr int kDecThreads = 128;
@@ -41,13 +44,50 @@ __device__ __forceinline__ void unpack16(const uint4& w, float* f) {
   }
 }
 
+// Where the candidate keys of a decode query come from.  total() candidates
+// t = 0 .. total()-1; key(t, &row) gives the cache row of candidate t and
+// whether the query sees it.
+//
+// PlanKeys: the kept 64-key tiles of mask row 0 (a full-length cache).
+struct PlanKeys {
+  MaskParams mp;
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  __device__ __forceinline__ int total() const { return (row_ptr[1] - row_ptr[0]) * kDecTile; }
+  __device__ __forceinline__ bool key(int t, int* row) const {
+    const int32_t ent = col_idx[row_ptr[0] + t / kDecTile];
+    const int kk = plan_index(ent) * kDecTile + (t % kDecTile);
+    *row = kk;
+    return visible(mp, 0, kk, plan_partial(ent));
+  }
+};
+
+// RingKeys: a StreamingLLM ring-buffer cache.  Rows [0, sink) hold positions
+// [0, sink); rows [sink, sink + window) hold positions p >= sink at
+// sink + (p - sink) % window.  The visible positions of the query at
+// seq_len - 1 are the n_sink sinks followed by the n_win window positions,
+// whose first one sits at ring offset slot0; all of them are visible.
+struct RingKeys {
+  int n_sink, n_win, slot0, sink, window;
+  __device__ __forceinline__ int total() const { return n_sink + n_win; }
+  __device__ __forceinline__ bool key(int t, int* row) const {
+    if (t < n_sink) {
+      *row = t;
+    } else {
+      int x = slot0 + (t - n_sink);
+      if (x >= window) x -= window;
+      *row = sink + x;
+    }
+    return true;
+  }
+};
+
 // Partial record layout in the workspace: [m, l, acc[0..D)] floats.
-template <typename T, int G>
+template <typename T, int G, typename Keys>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     T* __restrict__ o, float* __restrict__ lse, float* __restrict__ ws, int D, float scale,
-    MaskParams mp, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
-    int nsplit) {
+    Keys keys, int64_t kv_rows, int nsplit) {
   constexpr int EPV = 16 / sizeof(T);      // elements per 16-byte vector
   constexpr int GPW = 32 / G;              // lane groups per warp
   constexpr int NG = (kDecThreads / 32) * GPW;
@@ -68,13 +108,13 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
 #pragma unroll
     for (int i = 0; i < EPV; ++i) qv[i] *= scale;
   }
-  const int n_tiles = row_ptr[1] - row_ptr[0];
-  const int per = (n_tiles + nsplit - 1) / nsplit;
-  const int t0 = row_ptr[0] + split * per;
-  const int t1 = min(row_ptr[0] + n_tiles, t0 + per);
-  const int total = max(0, t1 - t0) * kDecTile;
-  const uint4* kb = reinterpret_cast<const uint4*>(k + bh * (size_t)mp.n_kv * D);
-  const uint4* vb = reinterpret_cast<const uint4*>(v + bh * (size_t)mp.n_kv * D);
+  // this split's candidates: [t_lo, t_hi), in whole 64-key tiles
+  const int all = keys.total();
+  const int per = ((all + nsplit - 1) / nsplit + kDecTile - 1) / kDecTile * kDecTile;
+  const int t_lo = split * per;
+  const int total = max(0, min(all, t_lo + per) - t_lo);
+  const uint4* kb = reinterpret_cast<const uint4*>(k + bh * (size_t)kv_rows * D);
+  const uint4* vb = reinterpret_cast<const uint4*>(v + bh * (size_t)kv_rows * D);
   const int vec_per_row = D / EPV;   // == G
 
   float m = -INFINITY, l = 0.f, acc[EPV];
@@ -90,9 +130,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
       const int t = base + u * NG + gid;
       vis[u] = false;
       if (t < total) {
-        const int32_t ent = col_idx[t0 + t / kDecTile];
-        const int key = plan_index(ent) * kDecTile + (t % kDecTile);
-        vis[u] = visible(mp, 0, key, plan_partial(ent));
+        int key = 0;
+        vis[u] = keys.key(t_lo + t, &key);
         if (vis[u]) {
           kw[u] = __ldg(kb + (size_t)key * vec_per_row + gl);
           vw[u] = __ldg(vb + (size_t)key * vec_per_row + gl);
@@ -196,13 +235,13 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws, T* __restrict_
   if (threadIdx.x == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
 }
 
-template <typename T, int G>
+template <typename T, int G, typename Keys>
 int launch_decode(const void* q, const void* k, const void* v, void* o, float* lse, float* ws,
-                  int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
-                  const int32_t* ci, int nsplit, cudaStream_t s) {
+                  int BH, int D, float scale, const Keys& keys, int64_t kv_rows, int nsplit,
+                  cudaStream_t s) {
   constexpr int NG = (kDecThreads / 32) * (32 / G);
   const size_t sm = sizeof(float) * NG * D;
-  auto kern = decode_split_kernel<T, G>;
+  auto kern = decode_split_kernel<T, G, Keys>;
   if (sm > 48 * 1024) {
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)sm), "cudaFuncSetAttribute(decode)"))
@@ -212,7 +251,7 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, float* l
   {
     LaunchScope ls("decode_split_kernel", s);
     kern<<<grid, kDecThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, ws,
-                                       D, scale, mp, rp, ci, nsplit);
+                                       D, scale, keys, kv_rows, nsplit);
   }
   if (int rc = check_launch("decode_split_kernel")) return rc;
   if (nsplit > 1) {
@@ -225,19 +264,39 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, float* l
   return SBFA_OK;
 }
 
-template <typename T>
+template <typename T, typename Keys>
 int dispatch_decode(int G, const void* q, const void* k, const void* v, void* o, float* lse,
-                    float* ws, int BH, int D, float scale, const MaskParams& mp,
-                    const int32_t* rp, const int32_t* ci, int nsplit, cudaStream_t s) {
+                    float* ws, int BH, int D, float scale, const Keys& keys, int64_t kv_rows,
+                    int nsplit, cudaStream_t s) {
   switch (G) {
-    case 1: return launch_decode<T, 1>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
-    case 2: return launch_decode<T, 2>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
-    case 4: return launch_decode<T, 4>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
-    case 8: return launch_decode<T, 8>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
-    case 16: return launch_decode<T, 16>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
-    case 32: return launch_decode<T, 32>(q, k, v, o, lse, ws, BH, D, scale, mp, rp, ci, nsplit, s);
+    case 1: return launch_decode<T, 1>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+    case 2: return launch_decode<T, 2>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+    case 4: return launch_decode<T, 4>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+    case 8: return launch_decode<T, 8>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+    case 16:
+      return launch_decode<T, 16>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+    case 32:
+      return launch_decode<T, 32>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
   }
   return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported head_dim for the vector layout");
+}
+
+template <typename Keys>
+int decode_any(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
+               void* ws, int BH, int D, float scale, const Keys& keys, int64_t kv_rows,
+               int nsplit, cudaStream_t s) {
+  const int G = decode_group(dtype, D);
+  float* w = (float*)ws;
+  switch (dtype) {
+    case SBFA_F16:
+      return dispatch_decode<__half>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows, nsplit, s);
+    case SBFA_BF16:
+      return dispatch_decode<__nv_bfloat16>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows,
+                                            nsplit, s);
+    case SBFA_F32:
+      return dispatch_decode<float>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows, nsplit, s);
+  }
+  return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported dtype");
 }
 
 }  // namespace
@@ -283,14 +342,8 @@ int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit) {
 int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
                const int32_t* ci, int nsplit, cudaStream_t s) {
-  const int G = decode_group(dtype, D);
-  float* w = (float*)ws;
-  switch (dtype) {
-    case SBFA_F16: return dispatch_decode<__half>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
-    case SBFA_BF16: return dispatch_decode<__nv_bfloat16>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
-    case SBFA_F32: return dispatch_decode<float>(G, q, k, v, o, lse, w, BH, D, scale, mp, rp, ci, nsplit, s);
-  }
-  return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported dtype");
+  const PlanKeys keys{mp, rp, ci};
+  return decode_any(dtype, q, k, v, o, lse, ws, BH, D, scale, keys, (int64_t)mp.n_kv, nsplit, s);
 }
 
 }  // namespace sbfa
@@ -365,4 +418,136 @@ extern "C" int sbfa_decode_noalloc(const void* q, const void* k, const void* v, 
   return sbfa_decode(q, k, v, o, lse, B, H, n_kv, head_dim, dtype, softmax_scale, is_causal, sink,
                      window, block_mask, block_m, block_n, row_ptr, col_idx,
                      ws_bytes > 0 ? base + plan_bytes : nullptr, ws_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// StreamingLLM ring-buffer KV cache
+// ---------------------------------------------------------------------------
+namespace sbfa {
+namespace {
+
+// Copies the new tokens' K and V rows into their ring rows, skipping the
+// positions a later token of the same call overwrites (so no two threads
+// write one row).  One 16-byte vector per thread and step.
+template <typename T>
+__global__ void ring_append_kernel(T* __restrict__ kc, T* __restrict__ vc,
+                                   const T* __restrict__ kn, const T* __restrict__ vn, int D,
+                                   int64_t rows, int64_t n_new, int64_t pos0, int64_t sink,
+                                   int64_t window) {
+  constexpr int kVec = 16 / sizeof(T);
+  const int vpr = D / kVec;
+  const int64_t bh = blockIdx.y;
+  const int64_t end = pos0 + n_new;
+  const int64_t n = n_new * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / vpr;
+    const int c = (int)(i % vpr);
+    const int64_t p = pos0 + t;
+    if (p >= sink && p < end - window) continue;  // overwritten within this call
+    const int64_t row = p < sink ? p : sink + (p - sink) % window;
+    const int64_t src = (bh * n_new + t) * D;
+    const int64_t dst = (bh * rows + row) * D;
+    reinterpret_cast<uint4*>(kc + dst)[c] = reinterpret_cast<const uint4*>(kn + src)[c];
+    reinterpret_cast<uint4*>(vc + dst)[c] = reinterpret_cast<const uint4*>(vn + src)[c];
+  }
+}
+
+RingKeys ring_keys(int64_t sink, int64_t window, int64_t seq_len) {
+  const int64_t n_sink = std::min(sink, seq_len);
+  const int64_t lo = std::max(sink, seq_len - window);
+  const int64_t n_win = std::max<int64_t>(0, seq_len - lo);
+  const int64_t slot0 = window > 0 ? (lo - sink) % window : 0;
+  return RingKeys{(int)n_sink, (int)n_win, (int)slot0, (int)sink, (int)window};
+}
+
+int check_ring(int64_t B, int64_t H, int64_t D, int dtype, int64_t sink, int64_t window) {
+  if (B <= 0 || H <= 0 || D <= 0)
+    return fail(SBFA_ERR_INVALID, "B, H and head_dim must be positive");
+  if (B * H > 65535) return fail(SBFA_ERR_UNSUPPORTED, "B * H must be <= 65535");
+  if (sink < 0 || window < 0)
+    return fail(SBFA_ERR_INVALID, "sink_size and window_size must be non-negative");
+  if (sink + window <= 0 || sink + window >= (1ll << 30))
+    return fail(SBFA_ERR_INVALID, "sink_size + window_size must be in [1, 2^30)");
+  if (decode_group(dtype, D) == 0)
+    return fail(SBFA_ERR_UNSUPPORTED,
+                "ring cache: dtype must be float16/bfloat16/float32 with head_dim * element "
+                "size a multiple of 16 bytes (at most 512 bytes)");
+  return SBFA_OK;
+}
+
+}  // namespace
+}  // namespace sbfa
+
+extern "C" int sbfa_ring_append(void* k_cache, void* v_cache, const void* k_new,
+                                const void* v_new, int64_t B, int64_t H, int64_t head_dim,
+                                int dtype, int64_t sink, int64_t window, int64_t pos0,
+                                int64_t n_new, void* stream) {
+  using namespace sbfa;
+  if (int rc = check_ring(B, H, head_dim, dtype, sink, window)) return rc;
+  if (!k_cache || !v_cache || !k_new || !v_new)
+    return fail(SBFA_ERR_INVALID, "sbfa_ring_append: NULL tensor pointer");
+  if (pos0 < 0 || n_new < 0) return fail(SBFA_ERR_INVALID, "pos0 and n_new must be >= 0");
+  if (n_new == 0) return SBFA_OK;
+  for (const void* p : {(const void*)k_cache, (const void*)v_cache, k_new, v_new})
+    if ((uintptr_t)p % 16) return fail(SBFA_ERR_INVALID, "ring cache tensors must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t rows = sink + window;
+  const int es = dtype == SBFA_F32 ? 4 : 2;
+  const int64_t vecs = n_new * (head_dim * es / 16);
+  dim3 grid((unsigned)std::min<int64_t>((vecs + 255) / 256, 1024), (unsigned)(B * H));
+  LaunchScope ls("ring_append_kernel", s);
+  switch (dtype) {
+    case SBFA_F16:
+      ring_append_kernel<__half><<<grid, 256, 0, s>>>((__half*)k_cache, (__half*)v_cache,
+                                                      (const __half*)k_new, (const __half*)v_new,
+                                                      (int)head_dim, rows, n_new, pos0, sink,
+                                                      window);
+      break;
+    case SBFA_BF16:
+      ring_append_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (const __nv_bfloat16*)k_new,
+          (const __nv_bfloat16*)v_new, (int)head_dim, rows, n_new, pos0, sink, window);
+      break;
+    case SBFA_F32:
+      ring_append_kernel<float><<<grid, 256, 0, s>>>((float*)k_cache, (float*)v_cache,
+                                                     (const float*)k_new, (const float*)v_new,
+                                                     (int)head_dim, rows, n_new, pos0, sink,
+                                                     window);
+      break;
+    default: return fail(SBFA_ERR_UNSUPPORTED, "ring cache: unsupported dtype");
+  }
+  return check_launch("ring_append_kernel");
+}
+
+extern "C" int64_t sbfa_ring_decode_workspace_bytes(int64_t B, int64_t H, int64_t head_dim,
+                                                    int64_t sink, int64_t window) {
+  using namespace sbfa;
+  if (B <= 0 || H <= 0 || head_dim <= 0 || sink < 0 || window < 0) return 0;
+  const int ns = decode_nsplit(B * H, (sink + window + kDecTile - 1) / kDecTile);
+  return decode_ws_bytes(B * H, head_dim, ns);
+}
+
+extern "C" int sbfa_ring_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
+                                float* lse, int64_t B, int64_t H, int64_t head_dim, int dtype,
+                                double softmax_scale, int64_t sink, int64_t window,
+                                int64_t seq_len, void* split_ws, int64_t split_ws_bytes,
+                                void* stream) {
+  using namespace sbfa;
+  if (int rc = check_ring(B, H, head_dim, dtype, sink, window)) return rc;
+  if (!q || !k_cache || !v_cache || !o)
+    return fail(SBFA_ERR_INVALID, "sbfa_ring_decode: NULL tensor pointer");
+  if (seq_len <= 0 || seq_len >= (1ll << 31))
+    return fail(SBFA_ERR_INVALID, "seq_len must be in [1, 2^31)");
+  for (const void* p : {q, k_cache, v_cache, (const void*)o})
+    if ((uintptr_t)p % 16) return fail(SBFA_ERR_INVALID, "ring cache tensors must be 16-byte aligned");
+  const RingKeys keys = ring_keys(sink, window, seq_len);
+  const int64_t BH = B * H;
+  const int ns = decode_nsplit(BH, (keys.n_sink + keys.n_win + kDecTile - 1) / kDecTile);
+  const int64_t need = decode_ws_bytes(BH, head_dim, ns);
+  if (need > 0 && (split_ws == nullptr || split_ws_bytes < need))
+    return fail(SBFA_ERR_INVALID, "sbfa_ring_decode: split workspace too small (need " +
+                                      std::to_string(need) + " bytes)");
+  return decode_any(dtype, q, k_cache, v_cache, o, lse, split_ws, (int)BH, (int)head_dim,
+                    (float)softmax_scale, keys, sink + window, ns, (cudaStream_t)stream);
 }

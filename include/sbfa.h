@@ -181,6 +181,39 @@ int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
  * run sbfa_fwd with n_q == 1, as upstream does). */
 int sbfa_decode_supported(int dtype, int64_t head_dim);
 
+/* ---------------------------------------------------------------------------
+ * StreamingLLM ring-buffer KV cache (no upstream counterpart: upstream keeps
+ * the whole cache and decodes through _fwd_kernel with N_Q = 1,
+ * benchmark.py:799-804).  The query at position p sees positions [0, sink)
+ * and (p - window, p], so a cache needs only sink + window rows per
+ * (batch, head): K and V caches are contiguous [B, H, sink + window, D];
+ * row r < sink holds position r, and position p >= sink lives in row
+ * sink + (p - sink) % window.  Same results as sbfa_decode over a full cache
+ * under the streaming rule (block mask with block_m = 1, causal), at
+ * (sink + window) / n_kv of its memory.
+ * ------------------------------------------------------------------------- */
+
+/* Writes K/V of positions [pos0, pos0 + n_new) (k_new, v_new: contiguous
+ * [B, H, n_new, D]) into their ring rows; positions that a later token of the
+ * same call would overwrite are skipped.  Positions must be appended in
+ * order across calls (pos0 = tokens already cached). */
+int sbfa_ring_append(void* k_cache, void* v_cache, const void* k_new, const void* v_new,
+                     int64_t B, int64_t H, int64_t head_dim, int dtype, int64_t sink,
+                     int64_t window, int64_t pos0, int64_t n_new, void* stream);
+
+/* Split-KV decode of the query at position seq_len - 1 (q, o: contiguous
+ * [B, H, 1, D]; lse may be NULL) over a ring cache holding positions
+ * [0, seq_len).  split_ws: caller scratch of
+ * sbfa_ring_decode_workspace_bytes() bytes (may be NULL when that is 0). */
+int sbfa_ring_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
+                     float* lse, int64_t B, int64_t H, int64_t head_dim, int dtype,
+                     double softmax_scale, int64_t sink, int64_t window, int64_t seq_len,
+                     void* split_ws, int64_t split_ws_bytes, void* stream);
+
+/* Scratch bytes sbfa_ring_decode needs for this cache geometry (any seq_len). */
+int64_t sbfa_ring_decode_workspace_bytes(int64_t B, int64_t H, int64_t head_dim, int64_t sink,
+                                         int64_t window);
+
 /* sbfa_decode without any device allocation by anyone.  No counterpart in
  * the upstream project, which has no decode entry point at all.
  *

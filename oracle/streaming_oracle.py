@@ -260,3 +260,19 @@ def visible_key_count(n_q: int, n_kv: int, block_mask, block_m: int, block_n: in
     bm = block_mask.cpu().numpy() if isinstance(block_mask, torch.Tensor) else block_mask
     return effective_token_mask(bm, n_q, n_kv, block_m, block_n, is_causal,
                                 sink, window).sum(axis=1)
+
+
+def ring_cache_positions(sink: int, window: int, seq_len: int) -> np.ndarray:
+    """Position held by each row of a StreamingLLM ring cache after positions
+    [0, seq_len) were appended in order (-1 = empty row).  Restates the
+    definition: the query at p sees [0, sink) and (p - window, p]
+    (upstream token rule, sparse_triton_kernel.py:315-320); row r < sink holds
+    position r, position p >= sink the row sink + (p - sink) % window, and a
+    later position overwrites an earlier one.  Test infrastructure."""
+    rows = np.full(sink + window, -1, dtype=np.int64)
+    for p in range(seq_len):
+        if p >= sink and window == 0:
+            continue  # never visible to a later query
+        r = p if p < sink else sink + (p - sink) % window
+        rows[r] = p
+    return rows
