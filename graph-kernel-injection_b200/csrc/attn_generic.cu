@@ -74,8 +74,8 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
   const T* qb = q + vw.at(vw.q, (int)bh, 0);
-  const T* kb = k + vw.at(vw.k, (int)bh, 0);
-  const T* vb = v + vw.at(vw.v, (int)bh, 0);
+  const T* kb = k + vw.at_kv(vw.k, (int)bh, 0);
+  const T* vb = v + vw.at_kv(vw.v, (int)bh, 0);
   const int row0 = ti * kRows;
   load_rows<T, A>(Qs, D, qb, vw.q.n, row0, kRows, mp.n_q, D);
 
@@ -235,8 +235,8 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
   const size_t bh = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
-  const T* kb = k + vw.at(vw.k, (int)bh, 0);
-  const T* vb = v + vw.at(vw.v, (int)bh, 0);
+  const T* kb = k + vw.at_kv(vw.k, (int)bh, 0);
+  const T* vb = v + vw.at_kv(vw.v, (int)bh, 0);
   const int row0 = ti * kRows;
   load_rows<T, A>(Qs, D, q + vw.at(vw.q, (int)bh, 0), vw.q.n, row0, kRows, mp.n_q, D);
   load_rows<T, A>(dOs, D, dout + vw.at(vw.dout, (int)bh, 0), vw.dout.n, row0, kRows, mp.n_q, D);
@@ -327,23 +327,28 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
   A* dOs = Qs + kKvRows * (D + 1);          // [kKvRows][D+1]
   A* Ls = dOs + kKvRows * (D + 1);          // [kKvRows]
   A* Dl = Ls + kKvRows;                     // [kKvRows]
+  // one CTA per (key tile, batch, key/value head): the query heads of the
+  // group all accumulate into the same dK, dV rows
   const int tj = blockIdx.x;
-  const size_t bh = blockIdx.y;
+  const int kv_heads = vw.heads / vw.kv_group;
+  const int bh0 = (int)(blockIdx.y / kv_heads) * vw.heads +
+                  (int)(blockIdx.y % kv_heads) * vw.kv_group;  // first query head's bh
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const A scale = (A)scale_f;
-  const T* qb = q + vw.at(vw.q, (int)bh, 0);
-  const T* gb = dout + vw.at(vw.dout, (int)bh, 0);
   const int key0 = tj * kKvKeys;
-  load_rows<T, A>(Ks, D, k + vw.at(vw.k, (int)bh, 0), vw.k.n, key0, kKvKeys, mp.n_kv, D);
-  load_rows<T, A>(Vs, D, v + vw.at(vw.v, (int)bh, 0), vw.v.n, key0, kKvKeys, mp.n_kv, D);
+  load_rows<T, A>(Ks, D, k + vw.at_kv(vw.k, bh0, 0), vw.k.n, key0, kKvKeys, mp.n_kv, D);
+  load_rows<T, A>(Vs, D, v + vw.at_kv(vw.v, bh0, 0), vw.v.n, key0, kKvKeys, mp.n_kv, D);
   A adk[4][DPL], adv[4][DPL];
 #pragma unroll
   for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int i = 0; i < DPL; ++i) adk[c][i] = adv[c][i] = 0;
-  const int e0 = col_ptr[tj], e1 = col_ptr[tj + 1];
-  for (int e = e0; e < e1; ++e) {
-    const int32_t ent = row_idx[e];
+  const int e0 = col_ptr[tj], ne = col_ptr[tj + 1] - e0;
+  for (int it = 0; it < ne * vw.kv_group; ++it) {
+    const int bh = bh0 + it / ne;
+    const T* qb = q + vw.at(vw.q, bh, 0);
+    const T* gb = dout + vw.at(vw.dout, bh, 0);
+    const int32_t ent = row_idx[e0 + it % ne];
     const int ti = plan_index(ent);
     const bool partial = plan_partial(ent);
     const int r0 = ti * kKvRows;
@@ -352,8 +357,8 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     load_rows<T, A>(dOs, D + 1, gb, vw.dout.n, r0, kKvRows, mp.n_q, D);
     for (int i = threadIdx.x; i < kKvRows; i += blockDim.x) {
       const int row = r0 + i;
-      Ls[i] = row < mp.n_q ? (A)lse[bh * mp.n_q + row] : A(0);
-      Dl[i] = row < mp.n_q ? (A)delta[bh * mp.n_q + row] : A(0);
+      Ls[i] = row < mp.n_q ? (A)lse[(int64_t)bh * mp.n_q + row] : A(0);
+      Dl[i] = row < mp.n_q ? (A)delta[(int64_t)bh * mp.n_q + row] : A(0);
     }
     __syncthreads();
 #pragma unroll
@@ -400,8 +405,8 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
       }
     }
   }
-  T* dkb = dk + vw.at(vw.dk, (int)bh, 0);
-  T* dvb = dv + vw.at(vw.dv, (int)bh, 0);
+  T* dkb = dk + vw.at_kv(vw.dk, bh0, 0);
+  T* dvb = dv + vw.at_kv(vw.dv, bh0, 0);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const int key = key0 + warp * 4 + c;
@@ -465,7 +470,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
     auto kern = dkdv_generic_kernel<T, DPL>;
     size_t sm = dkdv_smem<T>(D);
     if (int rc = set_smem(kern, sm)) return rc;
-    dim3 grid(ceil_div_i(mp.n_kv, kKvKeys), BH);
+    dim3 grid(ceil_div_i(mp.n_kv, kKvKeys), BH / vw.kv_group);
     {
       LaunchScope ls("dkdv_generic_kernel", s);
       kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
                   T* __restrict__ o, float* __restrict__ lse, float scale_log2, MaskParams mp,
                   const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
-                  int heads, Strides3 so, int* status) {
+                  int heads, int kv_group, Strides3 so, int* status) {
   using L = FwdLayout<D, STAGES>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescQK = idesc_f16(kBF16, kTM, kHalf, false, false);
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mbar_expect_tx(bar(L::kKVFull + s), L::kTile);
           for (int r = 0; r < kBoxes; ++r)
             tma_load_4d(sb + L::KV + s * L::kTile + r * 16384u, part == 0 ? &tmk : &tmv,
-                        bar(L::kKVFull + s), 64 * r, kt * kTN, hh, bb);
+                        bar(L::kKVFull + s), 64 * r, kt * kTN, hh / kv_group, bb);
           issued = e + 1;
         }
       }
@@ -420,9 +420,10 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t nh = (uint64_t)vw.heads, nb = (uint64_t)(BH / vw.heads);
+  const uint64_t nhk = nh / (uint64_t)vw.kv_group;  // key/value heads
   if (int rc = tc::make_tmap_4d(&mq, q, kBF16, D, (uint64_t)mp.n_q, nh, nb, vw.q, kTM)) return rc;
-  if (int rc = tc::make_tmap_4d(&mk, k, kBF16, D, (uint64_t)mp.n_kv, nh, nb, vw.k, kTN)) return rc;
-  if (int rc = tc::make_tmap_4d(&mv, v, kBF16, D, (uint64_t)mp.n_kv, nh, nb, vw.v, kTN)) return rc;
+  if (int rc = tc::make_tmap_4d(&mk, k, kBF16, D, (uint64_t)mp.n_kv, nhk, nb, vw.k, kTN)) return rc;
+  if (int rc = tc::make_tmap_4d(&mv, v, kBF16, D, (uint64_t)mp.n_kv, nhk, nb, vw.v, kTN)) return rc;
   if (int rc = tc::make_tmap_4d(&mo, o, kBF16, D, (uint64_t)mp.n_q, nh, nb, vw.o, kTM)) return rc;
   using L = FwdLayout<D, STAGES>;
   auto kern = fwd_tc_kernel<T, D, STAGES>;
@@ -434,7 +435,7 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
   {
     LaunchScope ls("fwd_tc_kernel", s);
     kern<<<grid, kFwdThreads, L::kAlloc, s>>>(mq, mk, mv, mo, (T*)o, lse, scale * kLog2e, mp, rp,
-                                             ci, vw.heads, vw.o, status);
+                                             ci, vw.heads, vw.kv_group, vw.o, status);
   }
   return check_launch("fwd_tc_kernel");
 }

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                    T* __restrict__ dv, const float* __restrict__ lse,
                    const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
                    const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
-                   int n_tj, int heads, Strides3 sdk, Strides3 sdv, int* status) {
+                   int n_tj, int heads, int kv_group, Strides3 sdk, Strides3 sdv, int* status) {
   using L = DkdvLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
@@ -128,9 +128,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the sink key tiles (seen by every query tile) first, one per (b, h);
-  // then each (b, h)'s remaining key tiles in order, so CTAs running side by
-  // side stream the same query tiles through L2
+  // BH counts (batch, key/value head) units.  The sink key tiles (seen by
+  // every query tile) first, one per unit; then each unit's remaining key
+  // tiles in order, so CTAs running side by side stream the same query tiles
+  // through L2.  With grouped-query attention the kv_group query heads of a
+  // unit are streamed one after another and all accumulate into its dK, dV.
   int tj, bh;
   if ((int)blockIdx.x < BH) {
     tj = 0;
@@ -140,9 +142,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bh = idx / (n_tj - 1);
     tj = 1 + idx % (n_tj - 1);
   }
-  const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
+  const int kv_heads = heads / kv_group;
+  const int hh = bh % kv_heads, bb = bh / kv_heads;  // TMA coordinates of the K/V plane
   const int e0 = col_ptr[tj];
-  const int nq = col_ptr[tj + 1] - e0;
+  const int nq = col_ptr[tj + 1] - e0;   // query tiles per query head
+  const int ntot = nq * kv_group;        // streamed tiles: (head j, tile) = (i / nq, i % nq)
 
   if (nq == 0) {  // no query sees this key tile: dK = dV = 0
     for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
@@ -200,9 +204,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int issued = 0;
       int next_ent = row_idx[e0];
       bool ok = true;
-      for (int i = 0; ok && i < nq; ++i) {
+      for (int i = 0; ok && i < ntot; ++i) {
         const int ti = plan_index(next_ent);
-        if (i + 1 < nq) next_ent = row_idx[e0 + i + 1];  // prefetch the next plan entry
+        const int hq = hh * kv_group + i / nq;  // query head of tile i
+        if (i + 1 < ntot) next_ent = row_idx[e0 + (i + 1) % nq];  // prefetch the next entry
         for (int part = 0; part < 2; ++part) {           // Q_i, then dO_i
           const int e = 2 * i + part, s = e % kRing, f = e / kRing;
           if (f > 0 && !wait_bar_w(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag,
@@ -214,7 +219,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             mbar_expect_tx(bar(L::kRFull + s), L::kTile);
             for (int r = 0; r < kBoxes; ++r)
               tma_load_4d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmdo : &tmq,
-                          bar(L::kRFull + s), 64 * r, ti * kT, hh, bb);
+                          bar(L::kRFull + s), 64 * r, ti * kT, hq, bb);
           }
           issued = e + 1;
         }
@@ -230,17 +235,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // ------------------------------------------- LSE (log2 units) / Delta
       // a warp of its own, so the latency of these loads never delays the
       // tensor copies
-      for (int i = 0; i < nq; ++i) {
+      for (int i = 0; i < ntot; ++i) {
         const int slot = i & 1;
-        const int ti = plan_index(row_idx[e0 + i]);
+        const int ti = plan_index(row_idx[e0 + i % nq]);
         const int row0 = ti * kT;
+        const size_t qbh = (size_t)bb * heads + hh * kv_group + i / nq;  // query (b, h)
         float lv[kT / 32], dv2[kT / 32];
 #pragma unroll
         for (int c = 0; c < kT / 32; ++c) {  // loads first, then the wait for the slot
           const int row = row0 + 32 * c + lane;
           const bool in = row < mp.n_q;
-          lv[c] = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
-          dv2[c] = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
+          lv[c] = in ? lse[qbh * mp.n_q + row] * kLog2e : 0.f;
+          dv2[c] = in ? delta[qbh * mp.n_q + row] : 0.f;
         }
         if (i >= 2 && !wait_bar_w(bar(L::kLEmpty + slot), (uint32_t)(((i >> 1) - 1) & 1),
                                   abort_flag, status))
@@ -296,13 +302,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         scores(kTDP, d_v, 1);  // dP_0
         tc_commit_w(bar(L::kDPFull));
       }
-      for (int i = 0; ok && i < nq; ++i) {
+      for (int i = 0; ok && i < ntot; ++i) {
         const uint32_t ph = (uint32_t)(i & 1);
         if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
         tc_fence_after();
         accum(kTDV, kTS, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
         tc_commit_w(bar(L::kREmpty + (2 * i + 1) % kRing));
-        if (i + 1 < nq) {
+        if (i + 1 < ntot) {
           if (!ring(2 * i + 2)) break;
           scores(kTS, d_k, 2 * i + 2);  // S_{i+1}, after dV_i has read P_i
           tc_commit_w(bar(L::kSFull));
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
         accum(kTDK, kTDP, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
         tc_commit_w(bar(L::kREmpty + (2 * i) % kRing));
-        if (i + 1 < nq) {
+        if (i + 1 < ntot) {
           if (!ring(2 * i + 3)) break;
           scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dK_i has read dS_i
           tc_commit_w(bar(L::kDPFull));
@@ -331,11 +337,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
     int32_t ent_next = row_idx[e0];
-    for (int i = 0; i < nq; ++i) {
+    for (int i = 0; i < ntot; ++i) {
       const int slot = i & 1;
       const uint32_t ph = (uint32_t)(i & 1);
       const int32_t ent = ent_next;
-      if (i + 1 < nq) ent_next = row_idx[e0 + i + 1];  // in flight while this tile runs
+      if (i + 1 < ntot) ent_next = row_idx[e0 + (i + 1) % nq];  // in flight while this tile runs
       const int q0 = plan_index(ent) * kT + 64 * grp;
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, q0, 64, tj * kT, kT, plan_partial(ent));
@@ -501,7 +507,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  const __grid_constant__ CUtensorMap tmdq, T* __restrict__ dq,
                  const float* __restrict__ lse, const float* __restrict__ delta, float scale,
                  float scale_log2, MaskParams mp, const int32_t* __restrict__ row_ptr,
-                 const int32_t* __restrict__ col_idx, int heads, Strides3 sdq, int* status) {
+                 const int32_t* __restrict__ col_idx, int heads, int kv_group, Strides3 sdq,
+                 int* status) {
   using L = DqLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 q, N=128 keys
@@ -585,7 +592,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mbar_expect_tx(bar(L::kRFull + s), L::kTile);
           for (int r = 0; r < kBoxes; ++r)
             tma_load_4d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmk : &tmv,
-                        bar(L::kRFull + s), 64 * r, kt * kT, hh, bb);
+                        bar(L::kRFull + s), 64 * r, kt * kT, hh / kv_group, bb);
           issued = e + 1;
         }
       }
@@ -781,13 +788,14 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv;
   const uint64_t nh = (uint64_t)vw.heads, nb = (uint64_t)(BH / vw.heads);
+  const uint64_t nhk = nh / (uint64_t)vw.kv_group;  // key/value heads
   if (int rc = make_tmap_4d(&mq, q, kBF16, D, nq, nh, nb, vw.q, kT)) return rc;
   if (int rc = make_tmap_4d(&mdo, dout, kBF16, D, nq, nh, nb, vw.dout, kT)) return rc;
-  if (int rc = make_tmap_4d(&mk, k, kBF16, D, nkv, nh, nb, vw.k, kT)) return rc;
-  if (int rc = make_tmap_4d(&mv, v, kBF16, D, nkv, nh, nb, vw.v, kT)) return rc;
+  if (int rc = make_tmap_4d(&mk, k, kBF16, D, nkv, nhk, nb, vw.k, kT)) return rc;
+  if (int rc = make_tmap_4d(&mv, v, kBF16, D, nkv, nhk, nb, vw.v, kT)) return rc;
   if (int rc = make_tmap_4d(&mdq, dq, kBF16, D, nq, nh, nb, vw.dq, kT)) return rc;
-  if (int rc = make_tmap_4d(&mdk, dk, kBF16, D, nkv, nh, nb, vw.dk, kT)) return rc;
-  if (int rc = make_tmap_4d(&mdv, dv, kBF16, D, nkv, nh, nb, vw.dv, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdk, dk, kBF16, D, nkv, nhk, nb, vw.dk, kT)) return rc;
+  if (int rc = make_tmap_4d(&mdv, dv, kBF16, D, nkv, nhk, nb, vw.dv, kT)) return rc;
   const float sl = scale * kLog2e;
   {
     using L = DkdvLayout<D>;
@@ -797,10 +805,12 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
                             "cudaFuncSetAttribute(dkdv_tc)"))
       return rc;
     const int n_tj = ceil_div_i(mp.n_kv, kT);
+    const int units = BH / vw.kv_group;  // (batch, key/value head) pairs
     LaunchScope ls("dkdv_tc_kernel", s);
-    kern<<<n_tj * BH, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse,
-                                                  delta, scale, sl, mp, kv_cp, kv_ri, BH, n_tj,
-                                                  vw.heads, vw.dk, vw.dv, status);
+    kern<<<n_tj * units, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv,
+                                                     lse, delta, scale, sl, mp, kv_cp, kv_ri,
+                                                     units, n_tj, vw.heads, vw.kv_group, vw.dk,
+                                                     vw.dv, status);
   }
   if (int rc = check_launch("dkdv_tc_kernel")) return rc;
   {
@@ -813,7 +823,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     dim3 grid(ceil_div_i(mp.n_q, kT), BH);
     LaunchScope ls("dq_tc_kernel", s);
     kern<<<grid, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdq, (T*)dq, lse, delta, scale, sl,
-                                              mp, dq_rp, dq_ci, vw.heads, vw.dq, status);
+                                              mp, dq_rp, dq_ci, vw.heads, vw.kv_group, vw.dq,
+                                              status);
   }
   return check_launch("dq_tc_kernel");
 }

@@ -162,17 +162,23 @@ MaskParams make_mp(int64_t n_q, int64_t n_kv, int is_causal, int64_t sink, int64
 bool use_tc(int pass, int dtype, int64_t D) { return tc_supports(pass, dtype, D); }
 
 // Views of a call: strides == NULL means every tensor is contiguous
-// [B, H, N, D]; otherwise strides holds (batch, head, row) element strides for
-// each of the `count` tensors in the order of Views' members.
-int make_views(const int64_t* strides, int count, int64_t H, int64_t n_q, int64_t n_kv,
-               int64_t D, Views* vw) {
+// [B, H or H_kv, N, D]; otherwise strides holds (batch, head, row) element
+// strides for each of the `count` tensors in the order of Views' members.
+// kv_heads <= 0 means H (no grouping); else H must be a multiple of it.
+int make_views(const int64_t* strides, int count, int64_t H, int64_t kv_heads, int64_t n_q,
+               int64_t n_kv, int64_t D, Views* vw) {
+  if (kv_heads <= 0) kv_heads = H;
+  if (H % kv_heads != 0)
+    return fail(SBFA_ERR_INVALID, "the query head count must be a multiple of kv_heads");
   Strides3* dst[8] = {&vw->q, &vw->k, &vw->v, &vw->o, &vw->dout, &vw->dq, &vw->dk, &vw->dv};
-  const bool kv_rows[8] = {false, true, true, false, false, false, true, true};
+  const bool kv_side[8] = {false, true, true, false, false, false, true, true};
   vw->heads = (int)H;
+  vw->kv_group = (int)(H / kv_heads);
   for (int t = 0; t < 8; ++t) {
-    const int64_t n = kv_rows[t] ? n_kv : n_q;
+    const int64_t n = kv_side[t] ? n_kv : n_q;
+    const int64_t h = kv_side[t] ? kv_heads : H;
     if (strides == nullptr || t >= count) {
-      *dst[t] = Strides3{H * n * D, n * D, D};
+      *dst[t] = Strides3{h * n * D, n * D, D};
     } else {
       const int64_t* st = strides + 3 * t;
       if (st[0] < 0 || st[1] < 0 || st[2] < D)
@@ -200,7 +206,7 @@ int check_tma(const void* const* ptrs, const Strides3* const* st, int count, con
 
 using namespace sbfa;
 
-extern "C" int sbfa_abi_version(void) { return 2; }
+extern "C" int sbfa_abi_version(void) { return 3; }
 
 extern "C" int64_t sbfa_launch_count(void) { return g_launches.load(); }
 
@@ -296,14 +302,14 @@ extern "C" int sbfa_fwd(const void* q, const void* k, const void* v, void* o, fl
                         int dtype, double softmax_scale, int is_causal, int64_t sink,
                         int64_t window, const int32_t* block_mask, int64_t block_m,
                         int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
-                        const int64_t* strides, void* stream) {
+                        const int64_t* strides, int64_t kv_heads, void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
   if (!q || !k || !v || !o || !lse || !row_ptr || !col_idx)
     return fail(SBFA_ERR_INVALID, "sbfa_fwd: NULL tensor or plan pointer");
   Views vw;
-  if (int rc = make_views(strides, 4, H, n_q, n_kv, head_dim, &vw)) return rc;
+  if (int rc = make_views(strides, 4, H, kv_heads, n_q, n_kv, head_dim, &vw)) return rc;
   MaskParams mp = make_mp(n_q, n_kv, is_causal, sink, window, block_mask, block_m, block_n);
   cudaStream_t s = (cudaStream_t)stream;
   const int BH = (int)(B * H);
@@ -327,7 +333,8 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
                         int64_t sink, int64_t window, const int32_t* block_mask,
                         int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
                         const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
-                        const int32_t* kv_row_idx, const int64_t* strides, void* stream) {
+                        const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
+                        void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
@@ -336,7 +343,7 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
   if (!dq_row_ptr || !dq_col_idx || !kv_col_ptr || !kv_row_idx)
     return fail(SBFA_ERR_INVALID, "sbfa_bwd: NULL plan pointer");
   Views vw;
-  if (int rc = make_views(strides, 8, H, n_q, n_kv, head_dim, &vw)) return rc;
+  if (int rc = make_views(strides, 8, H, kv_heads, n_q, n_kv, head_dim, &vw)) return rc;
   MaskParams mp = make_mp(n_q, n_kv, is_causal, sink, window, block_mask, block_m, block_n);
   cudaStream_t s = (cudaStream_t)stream;
   const int BH = (int)(B * H);

@@ -72,13 +72,21 @@ struct Strides3 {
   int64_t b, h, n;
 };
 
-// Strides of every tensor of a call and the head count that splits the
-// flattened (batch, head) index bh into (bh / heads, bh % heads).
+// Strides of every tensor of a call, the query head count that splits the
+// flattened (batch, query head) index bh into (bh / heads, bh % heads), and
+// the grouped-query factor: query head h reads key/value head h / kv_group
+// (kv_group = 1 without grouping).  k, v, dk, dv have heads / kv_group heads.
 struct Views {
   Strides3 q, k, v, o, dout, dq, dk, dv;
   int heads;
+  int kv_group;
+  // element offset of row `row` of query-side tensor s for bh
   __host__ __device__ __forceinline__ int64_t at(const Strides3& s, int bh, int64_t row) const {
     return (int64_t)(bh / heads) * s.b + (int64_t)(bh % heads) * s.h + row * s.n;
+  }
+  // element offset of row `row` of key/value-side tensor s for query bh
+  __host__ __device__ __forceinline__ int64_t at_kv(const Strides3& s, int bh, int64_t row) const {
+    return (int64_t)(bh / heads) * s.b + (int64_t)((bh % heads) / kv_group) * s.h + row * s.n;
   }
 };
 

@@ -106,12 +106,13 @@ def _rotate_half(x: torch.Tensor) -> torch.Tensor:
 
 
 class _LlamaAttention(nn.Module):
-    def __init__(self, hidden: int, n_heads: int, max_seq: int, theta: float, **kw) -> None:
+    def __init__(self, hidden: int, n_heads: int, n_kv_heads: int, max_seq: int, theta: float,
+                 **kw) -> None:
         super().__init__()
-        self.n_heads, self.head_dim = n_heads, hidden // n_heads
+        self.n_heads, self.n_kv_heads, self.head_dim = n_heads, n_kv_heads, hidden // n_heads
         self.q_proj = nn.Linear(hidden, hidden, bias=False, **kw)
-        self.k_proj = nn.Linear(hidden, hidden, bias=False, **kw)
-        self.v_proj = nn.Linear(hidden, hidden, bias=False, **kw)
+        self.k_proj = nn.Linear(hidden, n_kv_heads * self.head_dim, bias=False, **kw)
+        self.v_proj = nn.Linear(hidden, n_kv_heads * self.head_dim, bias=False, **kw)
         self.o_proj = nn.Linear(hidden, hidden, bias=False, **kw)
         dev = kw.get("device")
         inv = 1.0 / theta ** (torch.arange(0, self.head_dim, 2, device=dev).float() / self.head_dim)
@@ -123,22 +124,23 @@ class _LlamaAttention(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         b, n, _ = x.shape
         q = self.q_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
-        k = self.k_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
-        v = self.v_proj(x).view(b, n, self.n_heads, self.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(b, n, self.n_kv_heads, self.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(b, n, self.n_kv_heads, self.head_dim).transpose(1, 2)
         cos = _rope_rows(self.cos, n, q.dtype)
         sin = _rope_rows(self.sin, n, q.dtype)
         q = q * cos + _rotate_half(q) * sin
         k = k * cos + _rotate_half(k) * sin
-        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                           enable_gqa=self.n_kv_heads != self.n_heads)
         return self.o_proj(o.transpose(1, 2).reshape(b, n, self.n_heads * self.head_dim))
 
 
 class _LlamaBlock(nn.Module):
-    def __init__(self, hidden: int, n_heads: int, mlp: int, max_seq: int, theta: float,
-                 **kw) -> None:
+    def __init__(self, hidden: int, n_heads: int, n_kv_heads: int, mlp: int, max_seq: int,
+                 theta: float, **kw) -> None:
         super().__init__()
         self.attn_norm = _RMSNorm(hidden, **kw)
-        self.attn = _LlamaAttention(hidden, n_heads, max_seq, theta, **kw)
+        self.attn = _LlamaAttention(hidden, n_heads, n_kv_heads, max_seq, theta, **kw)
         self.mlp_norm = _RMSNorm(hidden, **kw)
         self.gate = nn.Linear(hidden, mlp, bias=False, **kw)
         self.up = nn.Linear(hidden, mlp, bias=False, **kw)
@@ -154,17 +156,20 @@ class LlamaStyleDecoder(nn.Module):
     """Llama-style decoder (RMSNorm, RoPE, SwiGLU MLP, untied LM head) whose
     attention is ``F.scaled_dot_product_attention(..., is_causal=True)`` on
     ``[B, H, N, D]`` transposed views -- the SDPA shape the pass rewrites.
-    ``forward(ids) -> logits``.  Keyword arguments ``device`` / ``dtype``
-    place and type every parameter at construction."""
+    ``n_kv_heads`` < ``n_heads`` gives grouped-query attention
+    (``enable_gqa=True``).  ``forward(ids) -> logits``.  Keyword arguments
+    ``device`` / ``dtype`` place and type every parameter at construction."""
 
     def __init__(self, vocab: int = 32000, hidden: int = 4096, n_layers: int = 8,
                  n_heads: int = 32, mlp: int = 11008, max_seq: int = 32768,
-                 rope_theta: float = 10000.0, device=None, dtype=None) -> None:
+                 rope_theta: float = 10000.0, n_kv_heads: Optional[int] = None, device=None,
+                 dtype=None) -> None:
         super().__init__()
         kw = {"device": device, "dtype": dtype}
+        n_kv = n_heads if n_kv_heads is None else n_kv_heads
         self.embed = nn.Embedding(vocab, hidden, **kw)
         self.layers = nn.ModuleList(
-            _LlamaBlock(hidden, n_heads, mlp, max_seq, rope_theta, **kw)
+            _LlamaBlock(hidden, n_heads, n_kv, mlp, max_seq, rope_theta, **kw)
             for _ in range(n_layers))
         self.norm = _RMSNorm(hidden, **kw)
         self.lm_head = nn.Linear(hidden, vocab, bias=False, **kw)

@@ -203,7 +203,9 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_mask: tor
     N_KV = k.shape[2]
     if k.shape != v.shape:
         raise ValueError("K and V must share shape")
-    if k.shape[:2] != q.shape[:2] or k.shape[-1] != D:
+    # grouped-query attention (an extension: upstream requires equal head
+    # counts): K/V may have fewer heads than Q when they divide Q's count
+    if k.shape[0] != B or k.shape[-1] != D or H % k.shape[1] != 0:
         raise ValueError("Q/K/V batch/head/dim mismatch")
     if not (q.dtype == k.dtype == v.dtype):
         raise ValueError("Q/K/V must share dtype")
@@ -279,7 +281,8 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
         block_mask = block_mask.to(device=dev, dtype=torch.int32).contiguous()
         code = native.dtype_code(q.dtype)
         L = native.lib()
-        decode = N_Q == 1 and bool(L.sbfa_decode_supported(code, D))
+        kv_heads = int(k.shape[1])
+        decode = N_Q == 1 and kv_heads == H and bool(L.sbfa_decode_supported(code, D))
         if decode:  # the decode kernel reads contiguous q / k / v
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         else:       # strided views are read in place
@@ -306,7 +309,7 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                     B, H, N_Q, N_KV, D, code, float(softmax_scale), int(bool(is_causal)),
                     int(sink_size), int(window_size), block_mask.data_ptr(), block_m, block_n,
                     plan["row_ptr"].data_ptr(), plan["col_idx"].data_ptr(),
-                    _stride_array(q, k, v, o), stream), "fwd")
+                    _stride_array(q, k, v, o), kv_heads, stream), "fwd")
         ctx.save_for_backward(q, k, v, o, lse, block_mask)
         ctx.softmax_scale = float(softmax_scale)
         ctx.block_m = int(block_m)
@@ -342,7 +345,7 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                 ctx.block_m, ctx.block_n, p_dq["row_ptr"].data_ptr(),
                 p_dq["col_idx"].data_ptr(), p_kv["col_ptr"].data_ptr(),
                 p_kv["row_idx"].data_ptr(), _stride_array(q, k, v, o, do, dq, dk, dv),
-                native.stream_ptr(dev)), "bwd")
+                int(k.shape[1]), native.stream_ptr(dev)), "bwd")
         return dq, dk, dv, None, None, None, None, None, None, None
 
 

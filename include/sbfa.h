@@ -132,6 +132,12 @@ int sbfa_plan_tiles(int pass, int dtype, int64_t head_dim, int64_t n_q,
  * through TMA) every tensor must be 16-byte aligned and its strides positive
  * multiples of 8 elements, else SBFA_ERR_INVALID.  lse and delta_ws are always
  * contiguous [B, H, n_q].
+ *
+ * kv_heads: grouped-query attention (no upstream counterpart; upstream
+ * requires equal head counts, sparse_triton_kernel.py:636-641).  k, v, dk,
+ * dv have kv_heads heads and query head h reads key/value head
+ * h / (H / kv_heads); dk, dv sum over each group's query heads.  kv_heads <= 0
+ * means H.
  */
 
 /* Forward: O = softmax(Q K^T * scale  masked) V, LSE = natural-log
@@ -144,7 +150,7 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
              int dtype, double softmax_scale, int is_causal, int64_t sink,
              int64_t window, const int32_t* block_mask, int64_t block_m,
              int64_t block_n, const int32_t* row_ptr, const int32_t* col_idx,
-             const int64_t* strides, void* stream);
+             const int64_t* strides, int64_t kv_heads, void* stream);
 
 /* Backward: dQ, dK, dV (written, not accumulated) from Q, K, V, O, dO and
  * the forward's LSE.  Replaces _bwd_preprocess_kernel, _bwd_dkdv_kernel,
@@ -159,7 +165,8 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              int64_t sink, int64_t window, const int32_t* block_mask,
              int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
              const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
-             const int32_t* kv_row_idx, const int64_t* strides, void* stream);
+             const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
+             void* stream);
 
 /* Split-KV decode for n_q == 1 (the upstream path is _fwd_kernel with
  * N_Q = 1, BLOCK_M = 1: benchmark.py:799-804 -> sparse_triton_kernel.py:231).

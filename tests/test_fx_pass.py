@@ -241,3 +241,12 @@ def test_llama_style_decoder_rewritten():
     assert mods[0].softmax_scale == pytest.approx(0.25)
     ids = torch.randint(0, 100, (1, 64))
     assert model(ids).shape == (1, 64, 100)  # the original model is untouched and runs
+
+
+def test_llama_gqa_rewritten():
+    from fx_compiler_pass import LlamaStyleDecoder
+    model = LlamaStyleDecoder(vocab=100, hidden=64, n_layers=2, n_heads=4, n_kv_heads=2, mlp=128,
+                              max_seq=64)
+    gm = BlockSparseAttentionInjector(cfg()).transform(model)
+    assert sdpa_calls(gm) == 0 and injected(gm) == 2
+    assert model(torch.randint(0, 100, (1, 64))).shape == (1, 64, 100)

@@ -332,3 +332,34 @@ def test_unaligned_view_falls_back_to_copy():
     a = stk.block_sparse_attention(q, k, v, mask, **kw)
     b = stk.block_sparse_attention(q.contiguous(), k, v, mask, **kw)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype,D,H,Hkv", [(torch.bfloat16, 128, 4, 2), (torch.float16, 64, 6, 1),
+                                           (torch.float32, 64, 4, 2), (torch.bfloat16, 64, 3, 3)])
+def test_grouped_query_heads(dtype, D, H, Hkv):
+    """Grouped-query attention: K/V with H / g heads, query head h reading
+    key/value head h // g.  Equal to the oracle run on K/V repeated g times,
+    with dK/dV the sums over each group's query heads."""
+    B, n, S, W, bm = 2, 384, 4, 128, 64
+    g = torch.Generator(device=DEV).manual_seed(9)
+    q = torch.randn(B, H, n, D, generator=g, device=DEV, dtype=dtype)
+    k = torch.randn(B, Hkv, n, D, generator=g, device=DEV, dtype=dtype)
+    v = torch.randn(B, Hkv, n, D, generator=g, device=DEV, dtype=dtype)
+    do = torch.randn(B, H, n, D, generator=g, device=DEV, dtype=dtype)
+    mask = stk.make_streaming_mask(n, n, stk.StreamingMaskSpec(S, W), bm, bm, DEV)
+    qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = stk.block_sparse_attention(qq, kk, vv, mask, block_m=bm, block_n=bm, is_causal=True,
+                                   sink_size=S, window_size=W)
+    o.backward(do)
+    assert native.device_status() == 0
+    rep = H // Hkv
+    ke, ve = (t.repeat_interleave(rep, dim=1) for t in (k, v))
+    ro, rdq, rdk, rdv = orc.attention_forward_backward(
+        q.double().cpu(), ke.double().cpu(), ve.double().cpu(), do.double().cpu(), mask.cpu(),
+        block_m=bm, block_n=bm, is_causal=True, sink_size=S, window_size=W)
+    rdk = rdk.view(B, Hkv, rep, n, D).sum(2)
+    rdv = rdv.view(B, Hkv, rep, n, D).sum(2)
+    close(o, ro, dtype, "fwd")
+    close(qq.grad, rdq, dtype, "bwd")
+    close(kk.grad, rdk, dtype, "bwd")
+    close(vv.grad, rdv, dtype, "bwd")

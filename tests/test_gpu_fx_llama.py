@@ -22,11 +22,14 @@ def _rel(a, b):
     return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
 
 
-def test_llama_fx_end_to_end_matches_masked_sdpa(monkeypatch):
+@pytest.mark.parametrize("n_kv_heads", [2, 1])
+def test_llama_fx_end_to_end_matches_masked_sdpa(monkeypatch, n_kv_heads):
+    """n_kv_heads = 1: grouped-query attention (enable_gqa=True) through the
+    same pass and kernels."""
     torch.manual_seed(0)
     n, sink, window = 1024, 4, 256
     model = LlamaStyleDecoder(vocab=512, hidden=256, n_layers=2, n_heads=2, mlp=512, max_seq=n,
-                              device=DEV, dtype=torch.bfloat16)
+                              n_kv_heads=n_kv_heads, device=DEV, dtype=torch.bfloat16)
     cfg = InjectionConfig(seq_len_q=n, seq_len_kv=n, head_dim=128,
                           streaming=stk.StreamingMaskSpec(sink, window), block_m=64, block_n=64)
     fused = BlockSparseAttentionInjector(cfg).transform(model).to(DEV)
@@ -48,7 +51,7 @@ def test_llama_fx_end_to_end_matches_masked_sdpa(monkeypatch):
     orig = F.scaled_dot_product_attention
 
     def masked_sdpa(q, k, v, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, **kw):
-        return orig(q, k, v, attn_mask=tok, dropout_p=dropout_p, scale=scale)
+        return orig(q, k, v, attn_mask=tok, dropout_p=dropout_p, scale=scale, **kw)
 
     monkeypatch.setattr(torch.nn.functional, "scaled_dot_product_attention", masked_sdpa)
     lr, lossr, gr = step(model)

@@ -44,7 +44,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.sbfa_abi_version() == 2
+    assert lib.sbfa_abi_version() == 3
 
 
 def test_validation_errors_without_gpu(lib):
@@ -57,10 +57,10 @@ def test_validation_errors_without_gpu(lib):
     rc = lib.sbfa_build_plan(None, 4, 4, 1, 1, 1, 1, None, None, None, None, None, None)
     assert rc == 1 and "block_mask" in native.last_error()
     rc = lib.sbfa_fwd(None, None, None, None, None, 1, 1, 0, 4, 16, 0, 1.0, 1, 0, 0, None,
-                      16, 16, None, None, None, None)
+                      16, 16, None, None, None, 0, None)
     assert rc == 1
     rc = lib.sbfa_fwd(None, None, None, None, None, 1, 1, 4, 4, 16, 9, 1.0, 1, 0, 0, None,
-                      16, 16, None, None, None, None)
+                      16, 16, None, None, None, 0, None)
     assert rc == 1 and "dtype" in native.last_error()
 
 
