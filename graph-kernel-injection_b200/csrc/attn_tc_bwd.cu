@@ -576,13 +576,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_4d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
         tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
       }
-      int issued = 0;
+      int fills[kRing] = {};  // copies issued per ring slot
       int next_ent = col_idx[e0];
       bool ok = true;
       for (int j = 0; ok && j < nk; ++j) {
         const int kt = plan_index(next_ent);
         if (j + 1 < nk) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
-        for (int part = 0; part < 2; ++part) {           // V_j, then K_j
+        // K_j (entry 2j+1) before V_j (entry 2j): K_j is read first (by S(j),
+        // issued a tile before dP(j)), and its slot was freed earlier (by
+        // V_{j-2}, released as soon as dP(j-2) was issued).  Each slot is still
+        // filled in entry order, so the per-slot parities hold.
+        for (int part = 1; part >= 0; --part) {
           const int e = 2 * j + part, s = e % kRing, f = e / kRing;
           if (f > 0 &&
               !wait_bar(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status)) {
@@ -593,14 +597,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int r = 0; r < kBoxes; ++r)
             tma_load_4d(sb + L::RING + s * L::kTile + r * 16384u, part ? &tmk : &tmv,
                         bar(L::kRFull + s), 64 * r, kt * kT, hh / kv_group, bb);
-          issued = e + 1;
+          ++fills[s];
         }
       }
       wait_bar_drain(bar(L::kQFull), 0, status);
-      for (int s = 0; s < kRing; ++s) {
-        const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
-        if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
-      }
+      for (int s = 0; s < kRing; ++s)
+        if (fills[s]) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills[s] - 1) & 1), status);
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
       // base descriptors, built once; MMAs add constant offsets
