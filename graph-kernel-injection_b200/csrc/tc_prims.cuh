@@ -78,15 +78,6 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
 // ---------------------------------------------------------------------------
 // TMA (tiled, into this CTA's own shared memory)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y, int z, int w) {
   asm volatile(
@@ -98,14 +89,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 
 // TMA tiled store shared -> global (no reduction); completion tracked with
 // the bulk async-group of the issuing thread.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y,
-                                             int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(src), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int x, int y,
                                              int z, int w) {
   asm volatile(
@@ -160,32 +143,14 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (fp16/bf16 in, fp32 acc).
-__device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16; A is K-major in TMEM (row m
-// in lane m, two consecutive K elements per 32-bit column).
-__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Warp-wide forms of the two MMAs and of the commit: every lane of the warp
-// executes them with identical (warp-uniform) operands and one elected lane
-// issues the instruction, so the operands stay in uniform registers and the
-// issue costs a few instructions rather than a per-lane-to-uniform move per
-// operand.
+// tcgen05.mma kind::f16 (fp16/bf16 in, fp32 accumulate) and tcgen05.commit,
+// issued warp-wide: every lane of the warp executes them with identical
+// (warp-uniform) operands and one elected lane issues the instruction, so the
+// operands stay in uniform registers and the issue costs a few instructions.
+// _ss: D[tmem] (+)= A[smem desc] * B[smem desc]; _ts: A from TMEM (K-major,
+// row m in lane m, two consecutive K elements per 32-bit column).  The commit
+// arrives once on `bar` when every tcgen05 async op issued so far by the
+// elected thread has completed.
 __device__ __forceinline__ void mma_f16_ss_w(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
                                              uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -219,14 +184,6 @@ __device__ __forceinline__ void tc_commit_w(uint32_t bar) {
 __device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                            int* status) {
   return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag, status));
-}
-
-// Arrive once on `bar` when every tcgen05 async op issued so far by this
-// thread has completed.
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
 }
 
 // 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers.
