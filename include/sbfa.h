@@ -57,6 +57,13 @@ int sbfa_last_error(char* buf, size_t len);
  * dynamic shared memory window not 1024-byte aligned and wrote nothing). */
 int sbfa_device_status(int* status_out);
 
+/* Failure-path self-test (no upstream counterpart): launches one block
+ * whose bounded wait on a barrier that nothing completes gives up after
+ * limit_ns (1e6 .. 1e9), exactly as every pipeline wait of the tensor-core
+ * kernels does; it records status 1 for sbfa_device_status and returns, and
+ * the context stays usable. */
+int sbfa_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* Total kernel launches issued by this library in this process. */
 int64_t sbfa_launch_count(void);
 

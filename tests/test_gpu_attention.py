@@ -286,6 +286,27 @@ def test_tensor_core_path_empty_rows(dtype, D):
     assert native.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_more_queries_than_keys_streaming(dtype):
+    """n_q > n_kv under the bottom-right alignment: the first n_q - n_kv
+    query rows sit at negative positions and see no key under the
+    streaming mask, so they are zero with zero dQ; the rest match the
+    oracle (tensor-core path for bf16, generic path for fp32)."""
+    n_q, n_kv, s, w = 640, 400, 4, 96
+    q, k, v, do = _inputs(1, 2, n_q, n_kv, 128, dtype, seed=5)
+    mask = stk.make_streaming_mask(n_q, n_kv, stk.StreamingMaskSpec(s, w), 128, 128, DEV)
+    o, dq, dk, dv = run(q, k, v, mask, 128, 128, True, s, w, do=do)
+    ro, rdq, rdk, rdv = orc.attention_forward_backward(
+        q.double().cpu(), k.double().cpu(), v.double().cpu(), do.double().cpu(), mask.cpu(),
+        block_m=128, block_n=128, is_causal=True, sink_size=s, window_size=w)
+    dead = n_q - n_kv
+    assert torch.count_nonzero(o[:, :, :dead]).item() == 0
+    assert torch.count_nonzero(dq[:, :, :dead]).item() == 0
+    for a, b, kind in ((o, ro, "fwd"), (dq, rdq, "bwd"), (dk, rdk, "bwd"), (dv, rdv, "bwd")):
+        close(a, b, dtype, kind)
+    assert native.device_status() == 0
+
+
 @pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64),
                                      (torch.float32, 64), (torch.bfloat16, 96)])
 def test_strided_views_read_in_place(dtype, D):
