@@ -2,7 +2,7 @@
 //
 // Forward (replaces upstream _fwd_kernel, sparse_triton_kernel.py:231-352).
 // One CTA per (pair of 128-row query tiles A/B, batch*head), 384 threads in
-// three warpgroups (registers rebalanced with setmaxnreg: 64 / 208 / 208):
+// three warpgroups (registers rebalanced with setmaxnreg: 88 / 208 / 208):
 //   warp 0      TMA producer: Q_A, Q_B once, then K_j, V_j of every kept key
 //               tile (plan CSR row, 256x128 tiles) into one STAGES-deep ring
 //               that alternates K and V tiles;
@@ -46,8 +46,8 @@ constexpr int kPair = 2;   // query tiles per CTA
 constexpr int kTN = 128;   // keys per key tile
 constexpr int kHalf = 64;  // keys per half-step (one 64-column S slot)
 constexpr int kFwdThreads = 384;
-constexpr int kRegsCtl = 64;       // producer / MMA warpgroup
-constexpr int kRegsSoftmax = 208;  // each softmax warpgroup (128*64 + 256*208 <= 384*168)
+constexpr int kRegsCtl = 88;       // producer / MMA warpgroup (64 spills descriptor math)
+constexpr int kRegsSoftmax = 208;  // each softmax warpgroup (128*88 + 256*208 == 384*168)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;
@@ -268,6 +268,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t t_o = tmem + lane_base + 256u + 128u * x;
     const int U = 2 * n;
     float m_run = -INFINITY, l_run = 0.f;
+    bool settled = false;  // warp-uniform: every row of this warp has a finite running max
     bool ok = true;
     int32_t ent = 0, ent_next = col_idx[e0];
     for (int u = 0; u < U; ++u) {
@@ -290,22 +291,51 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tmem_ld32(t_s, sv);
       tmem_ld32(t_s + 32u, sv + 32);
       tmem_wait_ld();
-      // row maximum of the raw scores; scale * log2(e) > 0 is applied after
-      float rmax = -INFINITY;
-      if (all_vis) {
+      if (!all_vis) {
 #pragma unroll
-        for (int c = 0; c < kHalf; ++c) rmax = fmaxf(rmax, __uint_as_float(sv[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < kHalf; ++c) {
-          const float v = ((vis[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(sv[c]) : -INFINITY;
-          sv[c] = __float_as_uint(v);
-          rmax = fmaxf(rmax, v);
-        }
+        for (int c = 0; c < kHalf; ++c)
+          if (!((vis[c >> 5] >> (c & 31)) & 1u)) sv[c] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m_run, rmax * scale_log2);
+      if (!settled) {
+        // some row of this warp has seen no visible key yet: its running
+        // maximum starts at this step's maximum (stays -inf if none visible)
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
+#pragma unroll
+        for (int c = 8; c < kHalf; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sv[c]));
+        const float rm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        if (m_run == -INFINITY) m_run = rm * scale_log2;
+        settled = __all_sync(0xffffffffu, m_run != -INFINITY);
+      }
+      // Exponentials against the running maximum, with this step's maximum
+      // reduced alongside them: a row whose maximum grew by more than 2^8
+      // (rare after the first tiles) is redone below.  A row with nothing
+      // visible so far has only -inf scores, so m_use = 0 gives p = 0.
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float mx[8], acc[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kHalf / 2];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kHalf / 2; ++i) {
+        const float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
+        mx[i & 7] = fmaxf(mx[i & 7], fmaxf(s0, s1));
+        const float p0 = ex2(fmaf(s0, scale_log2, -m_use));
+        const float p1 = ex2(fmaf(s1, scale_log2, -m_use));
+        acc[i & 3] += p0 + p1;
+        pk[i] = pack2<T>(p0, p1);
+      }
+      const float rm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = rm * scale_log2;
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
-      if (__any_sync(0xffffffffu, need)) {
+      float rsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      if (!__any_sync(0xffffffffu, need)) {
+        tmem_st16(t_s, pk);
+        tmem_st16(t_s + 16u, pk + 16);
+      } else {
         // O_X holds PV_X(0 .. u-1) once PV_X(u-1) has completed; the S_X(u)
         // barrier already implies PV_X(u-2), so this parity wait is exact
         ok = __all_sync(0xffffffffu, u == 0 || wait_bar(bar(L::kPVDone + x),
@@ -314,7 +344,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const float alpha = need ? ex2(m_run - m_new) : 1.f;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t t[32];
           tmem_ld32(t_o + 32u * c, t);
@@ -323,27 +353,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
           tmem_st32(t_o + 32u * c, t);
         }
-      }
-      if (need) {
-        l_run *= ex2(m_run - m_new);
-        m_run = m_new;
-      }
-      if (m_run == -INFINITY) m_run = m_new;  // first visible key: O row and l are still 0
-      const bool dead = (m_run == -INFINITY);
-      float rsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kHalf / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 =
-              dead ? 0.f : ex2(fmaf(__uint_as_float(sv[32 * c + 2 * i]), scale_log2, -m_run));
-          const float p1 =
-              dead ? 0.f : ex2(fmaf(__uint_as_float(sv[32 * c + 2 * i + 1]), scale_log2, -m_run));
-          rsum += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
+        if (need) {
+          l_run *= alpha;
+          m_run = m_new;
         }
-        tmem_st16(t_s + 16u * c, pk);
+        // recompute P against the new maximum, 32 scores at a time from the
+        // slot (P chunk c overwrites score columns that chunk c has read)
+        rsum = 0.f;
+        const float m_re = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll 1
+        for (int c = 0; c < kHalf / 32; ++c) {
+          uint32_t t[32], w[16];
+          tmem_ld32(t_s + 32u * c, t);
+          tmem_wait_ld();
+          const uint32_t vb = c == 0 ? vis[0] : vis[1];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float s0 = ((vb >> (2 * i)) & 1u) ? __uint_as_float(t[2 * i]) : -INFINITY;
+            const float s1 = ((vb >> (2 * i + 1)) & 1u) ? __uint_as_float(t[2 * i + 1]) : -INFINITY;
+            const float p0 = ex2(fmaf(s0, scale_log2, -m_re));
+            const float p1 = ex2(fmaf(s1, scale_log2, -m_re));
+            rsum += p0 + p1;
+            w[i] = pack2<T>(p0, p1);
+          }
+          tmem_st16(t_s + 16u * c, w);
+        }
       }
       tmem_wait_st();
       l_run += rsum;

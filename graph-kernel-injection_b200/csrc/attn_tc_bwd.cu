@@ -37,8 +37,8 @@ using namespace tc;
 constexpr int kT = 128;        // rows of a resident / streamed tile
 constexpr int kRing = 5;       // streamed tiles in flight (shared-memory ring entries)
 constexpr int kBwdThreads = 384;
-constexpr int kRegsCtl = 64;
-constexpr int kRegsCompute = 208;  // 128*64 + 256*208 <= 384*168
+constexpr int kRegsCtl = 88;       // producer / MMA / staging warps (64 spills)
+constexpr int kRegsCompute = 208;  // 128*88 + 256*208 == 384*168: the whole launch pool
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 
@@ -617,7 +617,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         return true;
       };
       // scores: tdst[128 x 128] = A (resident, K-major) * ring entry e^T
-      auto scores = [&](uint32_t tdst, uint64_t da, int e) {
+      auto scores = [&](uint32_t tdst, uint64_t da_in, int e) {
+        const uint64_t da = opaque(da_in);
         const uint64_t db = desc_advance(d_r, (uint32_t)(e % kRing) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -657,8 +658,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint64_t mk = desc_advance(m_r, (uint32_t)((2 * j + 1) % kRing) * L::kTile);
-        const uint32_t ts = tmem + kTS0 + 128u * (uint32_t)(j & 1);
+        const uint64_t mk = opaque(desc_advance(m_r, (uint32_t)((2 * j + 1) % kRing) * L::kTile));
+        const uint32_t ts = (uint32_t)opaque(tmem + kTS0 + 128u * (uint32_t)(j & 1));
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)  // dQ += dS_j K_j
           mma_f16_ts_w(tmem + kTDQ, ts + a_col128(kk), desc_advance(mk, (uint32_t)kk * 2048u),
