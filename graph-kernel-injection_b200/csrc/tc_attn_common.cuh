@@ -28,49 +28,55 @@ __device__ __forceinline__ bool wait_bar_drain(uint32_t bar, uint32_t parity, in
 // masks on interior tiles.
 __device__ __forceinline__ bool block_all_visible(const MaskParams& mp, int q_lo, int nq, int k_lo,
                                                   int nk, bool partial) {
-  if (partial) return false;
+  // branch-free, so that callers can compute it inside straight-line code
   const int q_hi = q_lo + nq - 1, k_hi = k_lo + nk - 1;
-  if (q_hi >= mp.n_q || k_hi >= mp.n_kv) return false;
-  if (!mp.causal) return true;
-  if (mp.q_off + q_lo < k_hi) return false;  // a key after a query
-  if (k_hi < mp.sink) return true;           // sink keys only
-  return mp.q_off + q_hi - max(k_lo, mp.sink) < mp.window;
+  const bool inside = !partial & (q_hi < mp.n_q) & (k_hi < mp.n_kv);
+  const bool token = (mp.q_off + q_lo >= k_hi) &                        // no key after a query
+                     ((k_hi < mp.sink) |                                 // sink keys only
+                      (mp.q_off + q_hi - max(k_lo, mp.sink) < mp.window));
+  return inside & (!mp.causal | token);
 }
 
 // Visibility of the NCOL keys [k0, k0+NCOL) for one query row, bit c of
-// vis[c/32] = key k0 + c: sequence end, token rule when causal (at most two
-// intervals: sink and window), lifted block mask on partial tiles.
+// vis[c/32] = key k0 + c, from the sequence ends and, when causal, the token
+// rule (at most two intervals: sink and window).  Branch-free.
+template <int NCOL>
+__device__ __forceinline__ void row_token_visibility(uint32_t (&vis)[NCOL / 32],
+                                                     const MaskParams& mp, int row, int k0) {
+  constexpr int W = NCOL / 32;
+  const int end = row < mp.n_q ? min(mp.n_kv - k0, NCOL) : 0;
+  const int qpos = mp.q_off + row;
+  const int cend = min(end, qpos - k0 + 1);
+  const int hi1 = mp.causal ? min(cend, mp.sink - k0) : end;
+  const int lo2 = mp.causal ? max(qpos - mp.window + 1 - k0, 0) : 0;
+  const int hi2 = mp.causal ? cend : 0;
+#pragma unroll
+  for (int w = 0; w < W; ++w) vis[w] = range_bits(0, hi1, 32 * w) | range_bits(lo2, hi2, 32 * w);
+}
+
+// Clears the keys of zero user blocks of the lifted block mask (partial tiles).
+template <int NCOL>
+__device__ __forceinline__ void row_block_mask(uint32_t (&vis)[NCOL / 32], const MaskParams& mp,
+                                               int row, int k0) {
+  constexpr int W = NCOL / 32;
+  if (row >= mp.n_q) return;
+  const int32_t* mrow = mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb;
+  const int b0 = k0 / mp.block_n;
+  const int b1 = min((k0 + NCOL - 1) / mp.block_n, mp.n_kb - 1);
+  for (int b = b0; b <= b1; ++b) {
+    if (__ldg(mrow + b) != 0) continue;
+    const int lo = b * mp.block_n - k0, hi = lo + mp.block_n;
+#pragma unroll
+    for (int w = 0; w < W; ++w) vis[w] &= ~range_bits(lo, hi, 32 * w);
+  }
+}
+
+// Both of the above: the full visibility of one row's NCOL keys.
 template <int NCOL>
 __device__ __forceinline__ void row_visibility(uint32_t (&vis)[NCOL / 32], const MaskParams& mp,
                                                int row, int k0, bool partial) {
-  constexpr int W = NCOL / 32;
-  if (row >= mp.n_q) {
-#pragma unroll
-    for (int w = 0; w < W; ++w) vis[w] = 0u;
-    return;
-  }
-  const int end = min(mp.n_kv - k0, NCOL);
-  int lo1 = 0, hi1 = end, lo2 = 0, hi2 = 0;
-  if (mp.causal) {
-    const int qpos = mp.q_off + row;
-    const int cend = min(end, qpos - k0 + 1);
-    hi1 = min(cend, mp.sink - k0);
-    lo2 = max(qpos - mp.window + 1 - k0, 0);
-    hi2 = cend;
-  }
-#pragma unroll
-  for (int w = 0; w < W; ++w) vis[w] = range_bits(lo1, hi1, 32 * w) | range_bits(lo2, hi2, 32 * w);
-  if (partial) {
-    const int32_t* mrow = mp.block_mask + (size_t)(row / mp.block_m) * mp.n_kb;
-    const int b0 = k0 / mp.block_n;
-    const int b1 = min((k0 + NCOL - 1) / mp.block_n, mp.n_kb - 1);
-    for (int b = b0; b <= b1; ++b) {
-      if (__ldg(mrow + b) != 0) continue;
-      const int lo = b * mp.block_n - k0, hi = lo + mp.block_n;
-#pragma unroll
-      for (int w = 0; w < W; ++w) vis[w] &= ~range_bits(lo, hi, 32 * w);
-    }
-  }
+  row_token_visibility<NCOL>(vis, mp, row, k0);
+  if (partial) row_block_mask<NCOL>(vis, mp, row, k0);
 }
 
 

@@ -179,8 +179,6 @@ __device__ __forceinline__ void tc_commit_w(uint32_t bar) {
           bar)
       : "memory");
 }
-// Bounded wait executed by a whole warp; false on every lane if any lane's
-// wait failed.
 // The value itself, hidden from the optimiser: descriptor offsets derived
 // from it are then computed next to each MMA instead of being hoisted out of
 // the issue loop as dozens of loop-invariant registers.
@@ -189,6 +187,8 @@ __device__ __forceinline__ uint64_t opaque(uint64_t v) {
   return v;
 }
 
+// Bounded wait executed by a whole warp; false on every lane if any lane's
+// wait failed.
 __device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                            int* status) {
   return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag, status));
