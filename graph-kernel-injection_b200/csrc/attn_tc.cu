@@ -282,8 +282,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, row0 + x * kTM, kTM, k0, kHalf, partial);
       if (!all_vis) row_visibility<kHalf>(vis, mp, row, k0, partial);
-      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kSFull + 2 * x + h), (uint32_t)((u >> 1) & 1),
-                                            abort_flag, status));
+      ok = wait_bar_w(bar(L::kSFull + 2 * x + h), (uint32_t)((u >> 1) & 1), abort_flag, status);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_s = t_sx + 64u * h;
@@ -384,7 +383,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       mbar_arrive(bar(L::kPFull + 2 * x + h));
     }
-    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kOFull + x), 0, abort_flag, status));
+    if (ok) ok = wait_bar_w(bar(L::kOFull + x), 0, abort_flag, status);
     if (ok) {
       tc_fence_after();
       const bool valid = l_run > 0.f;

@@ -346,10 +346,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, q0, 64, tj * kT, kT, plan_partial(ent));
       if (!all_vis) col_visibility<64>(vis, mp, key, q0, plan_partial(ent));
-      ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(L::kLFull + slot), (uint32_t)((i >> 1) & 1), abort_flag,
-                               status) &&
-                          wait_bar(bar(L::kSFull), ph, abort_flag, status));
+      ok = wait_bar_w(bar(L::kLFull + slot), (uint32_t)((i >> 1) & 1), abort_flag, status) &&
+           wait_bar_w(bar(L::kSFull), ph, abort_flag, status);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_s = tmem + lane_base + kTS + 64u * grp;
@@ -394,7 +392,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(bar(L::kPReady));
       // dS = P * (dP - Delta), in two 32-column halves
-      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDPFull), ph, abort_flag, status));
+      ok = wait_bar_w(bar(L::kDPFull), ph, abort_flag, status);
       if (!ok) break;
       tc_fence_after();
       uint32_t dsk[32];
@@ -424,7 +422,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes
     // dK * scale (staged in V's buffer); both buffers are free once every
     // MMA is done
-    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
+    if (ok) ok = wait_bar_w(bar(L::kDone), 0, abort_flag, status);
     if (ok) {
       tc_fence_after();
       const uint32_t t_acc = tmem + lane_base + (grp == 0 ? kTDV : kTDK);
@@ -477,7 +475,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // share one ring of kRing entries, entry 2j = V_j and 2j+1 = K_j: V_j is
 // only read by dP(j) and is released early, so the ring refills with the
 // next tiles while dQ_j still reads K_j.
-// MMA order: S(0) dP(0) S(1) | dP(j+1), dQ_j, S(j+2) for j = 0, 1, ...
+// MMA order: S(0) dP(0) | [dP(j) read] S(j+1), dP(j+1); [dS_j ready] dQ_j
+// for j = 0, 1, ...: K_{j+1} is first needed when the compute groups have
+// read dP(j), a ring slot's time later than if S(j+1) followed dQ_{j-1}.
 // Compute group g takes keys [64g, 64g+64) of every tile and writes its
 // packed dS over S columns [64g, 64g+32) of the same slot.
 template <int D>
@@ -636,15 +636,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         scores(kTDP, d_g, 0);  // dP(0) = dO V_0^T
         tc_commit_w(bar(L::kSDFull));
         tc_commit_w(bar(L::kREmpty + 0));
-        if (nk > 1) {
-          ok = ring(3);
-          if (ok) scores(kTS0 + 128u, d_q, 3);  // S(1)
-        }
       }
       for (int j = 0; ok && j < nk; ++j) {
-        if (j + 1 < nk) {  // dP(j+1) once the compute groups have read dP(j)
+        if (j + 1 < nk) {  // S(j+1) and dP(j+1) once the compute groups have read dP(j)
           if (!wait_bar_w(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status) ||
-              !ring(2 * j + 2)) {
+              !ring(2 * j + 3)) {
+            ok = false;
+            break;
+          }
+          // S(j+1) goes into the slot dQ_{j-1} has read (MMAs run in order)
+          scores(kTS0 + 128u * (uint32_t)((j + 1) & 1), d_q, 2 * j + 3);
+          if (!ring(2 * j + 2)) {
             ok = false;
             break;
           }
@@ -665,13 +667,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mma_f16_ts_w(tmem + kTDQ, ts + a_col128(kk), desc_advance(mk, (uint32_t)kk * 2048u),
                        kIdescAcc, (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit_w(bar(L::kREmpty + (2 * j + 1) % kRing));
-        if (j + 2 < nk) {  // S(j+2) into the slot dQ_j just read (MMAs run in order)
-          if (!ring(2 * j + 5)) {
-            ok = false;
-            break;
-          }
-          scores(kTS0 + 128u * (uint32_t)(j & 1), d_q, 2 * j + 5);
-        }
       }
       tc_commit_w(bar(L::kDone));
       tc_commit_w(bar(L::kDrain));
@@ -697,8 +692,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, ti * kT, kT, k0, 64, plan_partial(ent));
       if (!all_vis) row_visibility<64>(vis, mp, row, k0, plan_partial(ent));
-      ok = __all_sync(0xffffffffu, wait_bar(bar(L::kSDFull + (j & 1)), (uint32_t)((j >> 1) & 1),
-                                            abort_flag, status));
+      ok = wait_bar_w(bar(L::kSDFull + (j & 1)), (uint32_t)((j >> 1) & 1), abort_flag, status);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_s = tmem + lane_base + kTS0 + 128u * (uint32_t)(j & 1) + 64u * grp;
@@ -741,7 +735,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(bar(L::kPReady + (j & 1)));
     }
     // epilogue: dQ columns [64*grp, 64*grp + 64) staged in Q's buffer
-    if (ok) ok = __all_sync(0xffffffffu, wait_bar(bar(L::kDone), 0, abort_flag, status));
+    if (ok) ok = wait_bar_w(bar(L::kDone), 0, abort_flag, status);
     if (ok && 64 * grp < D) {
       tc_fence_after();
       const uint32_t t_acc = tmem + lane_base + kTDQ + 64u * grp;

@@ -188,9 +188,12 @@ __device__ __forceinline__ uint64_t opaque(uint64_t v) {
 }
 
 // Bounded wait executed by a whole warp; false on every lane if any lane's
-// wait failed.
+// wait failed.  The common case, a phase that has already completed, takes a
+// uniform fast path (one try_wait and one vote, ~25 cycles) instead of the
+// divergence-safe loop (~75).
 __device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                            int* status) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
   return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag, status));
 }
 
