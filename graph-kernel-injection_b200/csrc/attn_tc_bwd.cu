@@ -56,24 +56,29 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
 // A CTA owns 128 keys and walks the query tiles that see them (CSC plan).
 // TMEM: S_i^T = K Q_i^T at 0-127, dP_i^T = V dO_i^T at 128-255, dV at 256,
 // dK at 384.  Compute group g (query columns [64g, 64g+64) of the tile)
-// writes P_i packed to 16 bits over S columns [64g, 64g+32) and dS_i over
-// dP columns [64g, 64g+32), i.e. over values it has already read.  MMAs
-// from one issuer run in order, so S_{i+1} follows dV_i (the reader of P_i)
-// and dP_{i+1} follows dK_i (the reader of dS_i) without further waits:
-//   [P_i ready] dV += P_i^T dO_i, S_{i+1},
+// loads its S columns and releases them at once (SFree), so S_{i+1} is
+// computed while the group runs the exponentials of step i; it writes P_i^T
+// (16-bit, 128-byte swizzle) to a shared-memory tile that dV reads, and dS_i
+// packed over dP columns [64g, 64g+32) (values it has already read), where
+// dK reads it.  MMAs from one issuer run in order:
+//   [S_i loaded] S_{i+1},  [P_i stored] dV += P_i^T dO_i,
 //   [dS_i ready] dK += dS_i^T Q_i, dP_{i+1}.
-// The MMAs for S_{i+1} run while the compute groups work on dS_i.
 // Streamed tiles share one ring of kRing entries, entry 2i = Q_i and
 // 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
 // dK once in the epilogue.
 template <int D>
 struct DkdvLayout {
+  // K, V, the P tile and a 4-entry ring of 128-column tiles fill 224 KB;
+  // 64-column tiles leave room for 6 ring entries
+  static constexpr int kRing = D > 64 ? 4 : 6;
   static constexpr uint32_t kTile = kT * D * 2;
+  static constexpr uint32_t kPTile = kT * kT * 2;            // P_i^T: 128 keys x 128 queries
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + kTile;
-  static constexpr uint32_t RING = V + kTile;               // kRing streamed tiles
-  static constexpr uint32_t LS = RING + kRing * kTile;      // 2 x 128 floats (LSE * log2 e)
-  static constexpr uint32_t DL = LS + 2 * kT * 4;           // 2 x 128 floats (Delta)
+  static constexpr uint32_t P = V + kTile;
+  static constexpr uint32_t RING = P + kPTile;               // kRing streamed tiles
+  static constexpr uint32_t LS = RING + kRing * kTile;       // 2 x 128 floats (LSE * log2 e)
+  static constexpr uint32_t DL = LS + 2 * kT * 4;            // 2 x 128 floats (Delta)
   static constexpr uint32_t BAR = DL + 2 * kT * 4;
   static constexpr int kKVFull = 0;
   static constexpr int kRFull = 1;                   // [kRing]
@@ -81,12 +86,14 @@ struct DkdvLayout {
   static constexpr int kLFull = 1 + 2 * kRing;       // [2] LSE / Delta slot staged
   static constexpr int kLEmpty = 3 + 2 * kRing;      // [2] slot read by the compute groups
   static constexpr int kSFull = 5 + 2 * kRing;       // S_i written
-  static constexpr int kDPFull = 6 + 2 * kRing;      // dP_i written
-  static constexpr int kPReady = 7 + 2 * kRing;      // P_i packed in TMEM
-  static constexpr int kDSReady = 8 + 2 * kRing;     // dS_i packed in TMEM
-  static constexpr int kDone = 9 + 2 * kRing;
-  static constexpr int kDrain = 10 + 2 * kRing;
-  static constexpr int kNumBars = 11 + 2 * kRing;
+  static constexpr int kSFree = 6 + 2 * kRing;       // S_i loaded by the compute groups
+  static constexpr int kDPFull = 7 + 2 * kRing;      // dP_i written
+  static constexpr int kPReady = 8 + 2 * kRing;      // P_i^T in shared memory
+  static constexpr int kPFree = 9 + 2 * kRing;       // dV_i has read P_i^T
+  static constexpr int kDSReady = 10 + 2 * kRing;    // dS_i packed in TMEM
+  static constexpr int kDone = 11 + 2 * kRing;
+  static constexpr int kDrain = 12 + 2 * kRing;
+  static constexpr int kNumBars = 13 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kBytes = MISC + 16;
   // D = 128 leaves no room to align the window by hand: the kernel checks
@@ -164,7 +171,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::kKVFull), 1);
-    for (int s = 0; s < kRing; ++s) {
+    for (int s = 0; s < L::kRing; ++s) {
       mbar_init(bar(L::kRFull + s), 1);
       mbar_init(bar(L::kREmpty + s), 1);
     }
@@ -173,8 +180,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(bar(L::kLEmpty + x), 256);
     }
     mbar_init(bar(L::kSFull), 1);
+    mbar_init(bar(L::kSFree), 256);
     mbar_init(bar(L::kDPFull), 1);
     mbar_init(bar(L::kPReady), 256);
+    mbar_init(bar(L::kPFree), 1);
     mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
@@ -209,7 +218,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int hq = hh * kv_group + i / nq;  // query head of tile i
         if (i + 1 < ntot) next_ent = row_idx[e0 + (i + 1) % nq];  // prefetch the next entry
         for (int part = 0; part < 2; ++part) {           // Q_i, then dO_i
-          const int e = 2 * i + part, s = e % kRing, f = e / kRing;
+          const int e = 2 * i + part, s = e % L::kRing, f = e / L::kRing;
           if (f > 0 && !wait_bar_w(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag,
                                    status)) {
             ok = false;
@@ -226,8 +235,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (lane == 0) {
         wait_bar_drain(bar(L::kKVFull), 0, status);
-        for (int s = 0; s < kRing; ++s) {
-          const int fills = issued > s ? (issued - 1 - s) / kRing + 1 : 0;
+        for (int s = 0; s < L::kRing; ++s) {
+          const int fills = issued > s ? (issued - 1 - s) / L::kRing + 1 : 0;
           if (fills) wait_bar_drain(bar(L::kRFull + s), (uint32_t)((fills - 1) & 1), status);
         }
       }
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t d_r = desc_kmajor(sb + L::RING);
       const uint64_t m_r = desc_mnmajor(sb + L::RING, 16384u);
       auto ring = [&](int e) -> bool {
-        if (!wait_bar_w(bar(L::kRFull + e % kRing), (uint32_t)((e / kRing) & 1), abort_flag,
+        if (!wait_bar_w(bar(L::kRFull + e % L::kRing), (uint32_t)((e / L::kRing) & 1), abort_flag,
                         status))
           return false;
         tc_fence_after();
@@ -275,7 +284,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       };
       // tdst[128 keys x 128 q] = A (K or V, K-major) * (ring entry e)^T
       auto scores = [&](uint32_t tdst, uint64_t da, int e) {
-        const uint64_t db = desc_advance(d_r, (uint32_t)(e % kRing) * L::kTile);
+        const uint64_t db = desc_advance(d_r, (uint32_t)(e % L::kRing) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
@@ -285,7 +294,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       };
       // tacc[128 keys x D] += packed A (TMEM columns tsrc + a_col128) * ring entry e
       auto accum = [&](uint32_t tacc, uint32_t tsrc, int e, bool acc) {
-        const uint64_t mb = desc_advance(m_r, (uint32_t)(e % kRing) * L::kTile);
+        const uint64_t mb = desc_advance(m_r, (uint32_t)(e % L::kRing) * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
           mma_f16_ts_w(tmem + tacc, tmem + tsrc + a_col128(kk),
@@ -302,21 +311,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         scores(kTDP, d_v, 1);  // dP_0
         tc_commit_w(bar(L::kDPFull));
       }
+      const uint64_t d_p = desc_kmajor(sb + L::P);
       for (int i = 0; ok && i < ntot; ++i) {
         const uint32_t ph = (uint32_t)(i & 1);
-        if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
-        tc_fence_after();
-        accum(kTDV, kTS, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
-        tc_commit_w(bar(L::kREmpty + (2 * i + 1) % kRing));
-        if (i + 1 < ntot) {
-          if (!ring(2 * i + 2)) break;
-          scores(kTS, d_k, 2 * i + 2);  // S_{i+1}, after dV_i has read P_i
+        if (i + 1 < ntot) {  // S_{i+1} as soon as the compute groups have loaded S_i
+          if (!wait_bar_w(bar(L::kSFree), ph, abort_flag, status) || !ring(2 * i + 2)) break;
+          scores(kTS, d_k, 2 * i + 2);
           tc_commit_w(bar(L::kSFull));
         }
+        if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
+        tc_fence_after();
+        {  // dV += P_i^T dO_i with P_i^T from shared memory
+          const uint64_t mb = desc_advance(m_r, (uint32_t)((2 * i + 1) % L::kRing) * L::kTile);
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk) {
+            const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+            mma_f16_ss_w(tmem + kTDV, desc_advance(d_p, off),
+                         desc_advance(mb, (uint32_t)kk * 2048u), kIdescAcc,
+                         (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit_w(bar(L::kPFree));
+        tc_commit_w(bar(L::kREmpty + (2 * i + 1) % L::kRing));  // dO_i: dP_i and dV_i done
         if (!wait_bar_w(bar(L::kDSReady), ph, abort_flag, status)) break;
         tc_fence_after();
         accum(kTDK, kTDP, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
-        tc_commit_w(bar(L::kREmpty + (2 * i) % kRing));
+        tc_commit_w(bar(L::kREmpty + (2 * i) % L::kRing));      // Q_i: S_i and dK_i done
         if (i + 1 < ntot) {
           if (!ring(2 * i + 3)) break;
           scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dK_i has read dS_i
@@ -361,6 +381,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld32(t_s, sv);
         tmem_ld32(t_s + 32u, sv + 32);
         tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar(L::kSFree));  // S_{i+1} may overwrite the slot
         if (all_vis) {
 #pragma unroll
           for (int q4 = 0; q4 < 16; ++q4) {
@@ -383,13 +405,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
         }
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = pack2<T>(p[2 * c], p[2 * c + 1]);
-        tmem_st32(t_s, pk);
       }
-      tmem_wait_st();
-      tc_fence_before();
+      // P_i^T row (this key, the group's 64 queries) into shared memory, once
+      // dV_{i-1} has read the previous tile
+      if (i > 0 && !wait_bar_w(bar(L::kPFree), (uint32_t)((i - 1) & 1), abort_flag, status)) {
+        ok = false;
+        break;
+      }
+      {
+        const uint32_t prow = sb + L::P + (uint32_t)grp * 16384u;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const uint32_t addr = prow + sw128_offset((uint32_t)r, 8u * (uint32_t)c8);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                       "r"(pack2<T>(p[8 * c8 + 0], p[8 * c8 + 1])),
+                       "r"(pack2<T>(p[8 * c8 + 2], p[8 * c8 + 3])),
+                       "r"(pack2<T>(p[8 * c8 + 4], p[8 * c8 + 5])),
+                       "r"(pack2<T>(p[8 * c8 + 6], p[8 * c8 + 7]))
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
       mbar_arrive(bar(L::kPReady));
       // dS = P * (dP - Delta), in two 32-column halves
       ok = wait_bar_w(bar(L::kDPFull), ph, abort_flag, status);
