@@ -56,27 +56,26 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
 // A CTA owns 128 keys and walks the query tiles that see them (CSC plan).
 // TMEM: S_i^T = K Q_i^T at 0-127, dP_i^T = V dO_i^T at 128-255, dV at 256,
 // dK at 384.  Compute group g (query columns [64g, 64g+64) of the tile)
-// loads its S columns and releases them at once (SFree), so S_{i+1} is
-// computed while the group runs the exponentials of step i; it writes P_i^T
-// (16-bit, 128-byte swizzle) to a shared-memory tile that dV reads, and dS_i
-// packed over dP columns [64g, 64g+32) (values it has already read), where
-// dK reads it.  MMAs from one issuer run in order:
-//   [S_i loaded] S_{i+1},  [P_i stored] dV += P_i^T dO_i,
-//   [dS_i ready] dK += dS_i^T Q_i, dP_{i+1}.
+// loads its S columns and releases them at once, so S_{i+1} is computed
+// while the group runs the exponentials of step i; once it has loaded its dP
+// columns it packs dS_i (16-bit) into dP columns [64g, 64g+32) and P_i into
+// [64g+32, 64g+64), where the accumulator MMAs read them as the A operand.
+// MMAs from one issuer run in order, so dP_{i+1} overwrites the columns
+// only after dV_i and dK_i have read them:
+//   [S_i loaded] S_{i+1},  [P_i, dS_i packed] dV += P_i^T dO_i,
+//   dK += dS_i^T Q_i, dP_{i+1}.
 // Streamed tiles share one ring of kRing entries, entry 2i = Q_i and
 // 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
 // dK once in the epilogue.
 template <int D>
 struct DkdvLayout {
-  // K, V, the P tile and a 4-entry ring of 128-column tiles fill 224 KB;
-  // 64-column tiles leave room for 6 ring entries
-  static constexpr int kRing = D > 64 ? 4 : 6;
+  // K, V and a 5-entry ring of 128-column tiles fill 224 KB; 64-column
+  // tiles leave room for 6 ring entries
+  static constexpr int kRing = D > 64 ? 5 : 6;
   static constexpr uint32_t kTile = kT * D * 2;
-  static constexpr uint32_t kPTile = kT * kT * 2;            // P_i^T: 128 keys x 128 queries
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + kTile;
-  static constexpr uint32_t P = V + kTile;
-  static constexpr uint32_t RING = P + kPTile;               // kRing streamed tiles
+  static constexpr uint32_t RING = V + kTile;               // kRing streamed tiles
   static constexpr uint32_t LS = RING + kRing * kTile;       // 2 x 128 floats (LSE * log2 e)
   static constexpr uint32_t DL = LS + 2 * kT * 4;            // 2 x 128 floats (Delta)
   static constexpr uint32_t BAR = DL + 2 * kT * 4;
@@ -88,12 +87,10 @@ struct DkdvLayout {
   static constexpr int kSFull = 5 + 2 * kRing;       // S_i written
   static constexpr int kSFree = 6 + 2 * kRing;       // S_i loaded by the compute groups
   static constexpr int kDPFull = 7 + 2 * kRing;      // dP_i written
-  static constexpr int kPReady = 8 + 2 * kRing;      // P_i^T in shared memory
-  static constexpr int kPFree = 9 + 2 * kRing;       // dV_i has read P_i^T
-  static constexpr int kDSReady = 10 + 2 * kRing;    // dS_i packed in TMEM
-  static constexpr int kDone = 11 + 2 * kRing;
-  static constexpr int kDrain = 12 + 2 * kRing;
-  static constexpr int kNumBars = 13 + 2 * kRing;
+  static constexpr int kDSReady = 8 + 2 * kRing;     // P_i and dS_i packed in TMEM
+  static constexpr int kDone = 9 + 2 * kRing;
+  static constexpr int kDrain = 10 + 2 * kRing;
+  static constexpr int kNumBars = 11 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kBytes = MISC + 16;
   // D = 128 leaves no room to align the window by hand: the kernel checks
@@ -182,8 +179,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kSFull), 1);
     mbar_init(bar(L::kSFree), 256);
     mbar_init(bar(L::kDPFull), 1);
-    mbar_init(bar(L::kPReady), 256);
-    mbar_init(bar(L::kPFree), 1);
     mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
@@ -311,7 +306,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         scores(kTDP, d_v, 1);  // dP_0
         tc_commit_w(bar(L::kDPFull));
       }
-      const uint64_t d_p = desc_kmajor(sb + L::P);
       for (int i = 0; ok && i < ntot; ++i) {
         const uint32_t ph = (uint32_t)(i & 1);
         if (i + 1 < ntot) {  // S_{i+1} as soon as the compute groups have loaded S_i
@@ -319,27 +313,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           scores(kTS, d_k, 2 * i + 2);
           tc_commit_w(bar(L::kSFull));
         }
-        if (!wait_bar_w(bar(L::kPReady), ph, abort_flag, status)) break;
-        tc_fence_after();
-        {  // dV += P_i^T dO_i with P_i^T from shared memory
-          const uint64_t mb = desc_advance(m_r, (uint32_t)((2 * i + 1) % L::kRing) * L::kTile);
-#pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {
-            const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-            mma_f16_ss_w(tmem + kTDV, desc_advance(d_p, off),
-                         desc_advance(mb, (uint32_t)kk * 2048u), kIdescAcc,
-                         (i > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        tc_commit_w(bar(L::kPFree));
-        tc_commit_w(bar(L::kREmpty + (2 * i + 1) % L::kRing));  // dO_i: dP_i and dV_i done
         if (!wait_bar_w(bar(L::kDSReady), ph, abort_flag, status)) break;
         tc_fence_after();
-        accum(kTDK, kTDP, 2 * i, i > 0);  // dK += dS_i^T Q_i (unscaled)
-        tc_commit_w(bar(L::kREmpty + (2 * i) % L::kRing));      // Q_i: S_i and dK_i done
+        accum(kTDV, kTDP + 32u, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
+        tc_commit_w(bar(L::kREmpty + (2 * i + 1) % L::kRing));
+        accum(kTDK, kTDP, 2 * i, i > 0);            // dK += dS_i^T Q_i (unscaled)
+        tc_commit_w(bar(L::kREmpty + (2 * i) % L::kRing));
         if (i + 1 < ntot) {
           if (!ring(2 * i + 3)) break;
-          scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dK_i has read dS_i
+          scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dV_i and dK_i have read P_i, dS_i
           tc_commit_w(bar(L::kDPFull));
         }
       }
@@ -357,11 +339,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
     int32_t ent_next = row_idx[e0];
+    int pos_next = nq > 1 ? 1 : 0;  // (i + 1) % nq, kept as a counter (no division)
     for (int i = 0; i < ntot; ++i) {
       const int slot = i & 1;
       const uint32_t ph = (uint32_t)(i & 1);
       const int32_t ent = ent_next;
-      if (i + 1 < ntot) ent_next = row_idx[e0 + (i + 1) % nq];  // in flight while this tile runs
+      if (i + 1 < ntot) ent_next = row_idx[e0 + pos_next];  // in flight while this tile runs
+      pos_next = pos_next + 1 == nq ? 0 : pos_next + 1;
       const int q0 = plan_index(ent) * kT + 64 * grp;
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, q0, 64, tj * kT, kT, plan_partial(ent));
@@ -406,27 +390,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       }
-      // P_i^T row (this key, the group's 64 queries) into shared memory, once
-      // dV_{i-1} has read the previous tile
-      if (i > 0 && !wait_bar_w(bar(L::kPFree), (uint32_t)((i - 1) & 1), abort_flag, status)) {
-        ok = false;
-        break;
-      }
-      {
-        const uint32_t prow = sb + L::P + (uint32_t)grp * 16384u;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          const uint32_t addr = prow + sw128_offset((uint32_t)r, 8u * (uint32_t)c8);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                       "r"(pack2<T>(p[8 * c8 + 0], p[8 * c8 + 1])),
-                       "r"(pack2<T>(p[8 * c8 + 2], p[8 * c8 + 3])),
-                       "r"(pack2<T>(p[8 * c8 + 4], p[8 * c8 + 5])),
-                       "r"(pack2<T>(p[8 * c8 + 6], p[8 * c8 + 7]))
-                       : "memory");
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(bar(L::kPReady));
       // dS = P * (dP - Delta), in two 32-column halves
       ok = wait_bar_w(bar(L::kDPFull), ph, abort_flag, status);
       if (!ok) break;
@@ -450,6 +413,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       mbar_arrive(bar(L::kLEmpty + slot));  // the LSE / Delta slot has been read
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = pack2<T>(p[2 * c], p[2 * c + 1]);
+        tmem_st32(t_dp + 32u, pk);  // P_i over dP columns [64g+32, 64g+64), already read
+      }
       tmem_st32(t_dp, dsk);
       tmem_wait_st();
       tc_fence_before();
