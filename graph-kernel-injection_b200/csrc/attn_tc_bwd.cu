@@ -358,8 +358,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t t_dp = tmem + lane_base + kTDP + 64u * grp;
       const float4* ls4 = reinterpret_cast<const float4*>(smem + L::LS) + (slot * kT + 64 * grp) / 4;
       const float4* dl4 = reinterpret_cast<const float4*>(smem + L::DL) + (slot * kT + 64 * grp) / 4;
-      // P = 2^(S * scale * log2 e - LSE * log2 e) on visible pairs
+      // P = 2^(S * scale * log2 e - LSE * log2 e) on visible pairs, packed to
+      // 16 bits while the exponentials are in flight
       float p[64];
+      uint32_t pk[32];
       {
         uint32_t sv[64];
         tmem_ld32(t_s, sv);
@@ -389,6 +391,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
         }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = pack2<T>(p[2 * c], p[2 * c + 1]);
       }
       // dS = P * (dP - Delta), in two 32-column halves
       ok = wait_bar_w(bar(L::kDPFull), ph, abort_flag, status);
@@ -413,12 +417,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       mbar_arrive(bar(L::kLEmpty + slot));  // the LSE / Delta slot has been read
-      {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = pack2<T>(p[2 * c], p[2 * c + 1]);
-        tmem_st32(t_dp + 32u, pk);  // P_i over dP columns [64g+32, 64g+64), already read
-      }
+      tmem_st32(t_dp + 32u, pk);  // P_i over dP columns [64g+32, 64g+64), already read
       tmem_st32(t_dp, dsk);
       tmem_wait_st();
       tc_fence_before();
