@@ -35,7 +35,7 @@ namespace {
 using namespace tc;
 
 constexpr int kT = 128;        // rows of a resident / streamed tile
-constexpr int kRing = 5;       // streamed tiles in flight (shared-memory ring entries)
+constexpr int kRing = 5;       // dQ ring entries (streamed tiles in flight); DkdvLayout sets its own
 constexpr int kBwdThreads = 384;
 constexpr int kRegsCtl = 88;       // producer / MMA / staging warps (64 spills)
 constexpr int kRegsCompute = 208;  // 128*88 + 256*208 == 384*168: the whole launch pool
