@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
 // is a whole number of 16-byte vectors (D * sizeof(T) % 16 == 0, at most 32
 // of them), `g` = D / vec lanes share a row with one vector load each and
 // 32 / g rows run per warp; otherwise a warp takes a row with scalar loads.
+constexpr int kDeltaRows = 4;  // rows per lane group in the vectorised Delta path
+
 template <typename T>
 __global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ dout,
                              float* __restrict__ delta, int n_q, int D, int g, Views vw) {
@@ -171,20 +173,35 @@ __global__ void delta_kernel(const T* __restrict__ o, const T* __restrict__ dout
   const T* gb = dout + vw.at(vw.dout, bh, 0);
   float* db = delta + (int64_t)bh * n_q;
   if (g > 0) {
+    // kDeltaRows rows per lane group, all loads issued before any use so each
+    // thread keeps 2 * kDeltaRows 16-byte loads in flight
     const int per_warp = 32 / g;
-    const int row = (blockIdx.x * (blockDim.x >> 5) + warp) * per_warp + lane / g;
+    const int rows_per_block = (blockDim.x >> 5) * per_warp;
+    const int row0 = (blockIdx.x * kDeltaRows * (blockDim.x >> 5) + warp) * per_warp + lane / g;
     const int sub = lane % g;
-    A s = 0;
-    if (row < n_q) {
-      const uint4 a = *reinterpret_cast<const uint4*>(ob + (int64_t)row * vw.o.n + sub * kVec);
-      const uint4 b = *reinterpret_cast<const uint4*>(gb + (int64_t)row * vw.dout.n + sub * kVec);
-      const T* ta = reinterpret_cast<const T*>(&a);
-      const T* tb = reinterpret_cast<const T*>(&b);
+    uint4 a[kDeltaRows], b[kDeltaRows];
+#pragma unroll
+    for (int k = 0; k < kDeltaRows; ++k) {
+      const int row = row0 + k * rows_per_block;
+      if (row < n_q) {
+        a[k] = *reinterpret_cast<const uint4*>(ob + (int64_t)row * vw.o.n + sub * kVec);
+        b[k] = *reinterpret_cast<const uint4*>(gb + (int64_t)row * vw.dout.n + sub * kVec);
+      } else {
+        a[k] = make_uint4(0, 0, 0, 0);
+        b[k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kDeltaRows; ++k) {
+      const int row = row0 + k * rows_per_block;
+      const T* ta = reinterpret_cast<const T*>(&a[k]);
+      const T* tb = reinterpret_cast<const T*>(&b[k]);
+      A s = 0;
 #pragma unroll
       for (int i = 0; i < kVec; ++i) s += Elem<T>::to(ta[i]) * Elem<T>::to(tb[i]);
+      for (int off = g >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (row < n_q && sub == 0) db[row] = (float)s;
     }
-    for (int off = g >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (row < n_q && sub == 0) db[row] = (float)s;
   } else {
     const int row = blockIdx.x * (blockDim.x >> 5) + warp;
     if (row >= n_q) return;
@@ -207,7 +224,7 @@ int launch_delta(const void* o, const void* dout, float* delta, int BH, int n_q,
                       vw.o.n % kVec == 0 && vw.o.h % kVec == 0 && vw.o.b % kVec == 0 &&
                       vw.dout.n % kVec == 0 && vw.dout.h % kVec == 0 && vw.dout.b % kVec == 0;
   const int g = vec_ok ? D / kVec : 0;
-  const int rows_per_block = 8 * (g > 0 ? 32 / g : 1);
+  const int rows_per_block = g > 0 ? 8 * (32 / g) * kDeltaRows : 8;
   dim3 grid(ceil_div_i(n_q, rows_per_block), BH);
   {
     LaunchScope ls("delta_kernel", s);
