@@ -309,18 +309,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int i = 0; ok && i < ntot; ++i) {
         const uint32_t ph = (uint32_t)(i & 1);
         if (i + 1 < ntot) {  // S_{i+1} as soon as the compute groups have loaded S_i
-          if (!wait_bar_w(bar(L::kSFree), ph, abort_flag, status) || !ring(2 * i + 2)) break;
+          if (!ring(2 * i + 2) || !wait_bar_w(bar(L::kSFree), ph, abort_flag, status)) break;
+          tc_fence_after();
           scores(kTS, d_k, 2 * i + 2);
           tc_commit_w(bar(L::kSFull));
         }
-        if (!wait_bar_w(bar(L::kDSReady), ph, abort_flag, status)) break;
+        // dO_{i+1} is checked before the wait for dS_i, off the critical path
+        if ((i + 1 < ntot && !ring(2 * i + 3)) ||
+            !wait_bar_w(bar(L::kDSReady), ph, abort_flag, status))
+          break;
         tc_fence_after();
         accum(kTDV, kTDP + 32u, 2 * i + 1, i > 0);  // dV += P_i^T dO_i
         tc_commit_w(bar(L::kREmpty + (2 * i + 1) % L::kRing));
         accum(kTDK, kTDP, 2 * i, i > 0);            // dK += dS_i^T Q_i (unscaled)
         tc_commit_w(bar(L::kREmpty + (2 * i) % L::kRing));
         if (i + 1 < ntot) {
-          if (!ring(2 * i + 3)) break;
           scores(kTDP, d_v, 2 * i + 3);  // dP_{i+1}, after dV_i and dK_i have read P_i, dS_i
           tc_commit_w(bar(L::kDPFull));
         }
@@ -643,11 +646,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk) {  // S(j+1) and dP(j+1) once the compute groups have read dP(j)
-          if (!wait_bar_w(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status) ||
-              !ring(2 * j + 3)) {
+          // K_{j+1} is checked first, while the compute groups are still on
+          // dP(j), so the check stays off the critical path
+          if (!ring(2 * j + 3) ||
+              !wait_bar_w(bar(L::kDPFree), (uint32_t)(j & 1), abort_flag, status)) {
             ok = false;
             break;
           }
+          tc_fence_after();
           // S(j+1) goes into the slot dQ_{j-1} has read (MMAs run in order)
           scores(kTS0 + 128u * (uint32_t)((j + 1) & 1), d_q, 2 * j + 3);
           if (!ring(2 * j + 2)) {
