@@ -6,10 +6,14 @@
 Headline (``value``): BASELINE config 2 -- sparse prefill forward+backward,
 B=4, H=32, N=16384, D=128, bf16, S=4, W=2048, BM=BN=128 -- as kept-block
 TFLOP/s (F_fwd = nnz * B * H * 4 * BM * BN * D; fwd+bwd = 3.5 * F_fwd).
-Each rank processes its own B*H = 128 (batch, head) units (weak scaling:
-the job's batch is 4 * N); ``value`` = all ranks' FLOPs / max-over-ranks
-time.  Secondary lines (``extra``): config 3 prefill forward (TFLOP/s) and
-config 4 decode (KV GB/s over the 2.1517e9 visible K/V bytes per step).
+The problem is fixed and its B*H = 128 (batch, head) units are split
+contiguously across the N ranks (strong scaling, no collective on the data
+path); ``value`` = the whole problem's FLOPs / max-over-ranks time.  After
+the timed region O, dQ, dK, dV are all-gathered (NCCL) and compared bit for
+bit with a single-GPU run on rank 0.  Secondary lines (``extra``): config 3
+prefill forward (TFLOP/s), config 4 decode (KV GB/s over the 2.1517e9
+visible K/V bytes per step), both split the same way, and config 5 (the FX
+pass on an 8-layer Llama-style decoder, one GPU).
 
 ``e2e`` runs the same step through the public API from pinned host buffers
 (Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step).
@@ -43,6 +47,8 @@ CFG3 = dict(B=1, H=32, N=131072, D=128, S=4, W=4096, BM=128, BN=128, dtype=torch
 CFG4 = dict(B=64, H=32, N=100001, D=128, S=4, W=2048, BM=1, BN=64, dtype=torch.float16)
 CFG5 = dict(B=2, N=32768, hidden=4096, layers=8, H=32, D=128, mlp=11008, vocab=32000, S=4,
             W=2048, BM=64, BN=64, dtype=torch.bfloat16)
+
+GQA_GROUP = 4   # query heads per K/V head in the grouped-query decode line
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -85,10 +91,6 @@ class Dist:
     def max(self, x: float) -> float:
         import shard
         return shard.max_over_ranks(x)
-
-    def gather_checksums(self, vals):
-        import shard
-        return shard.gather_values(vals)
 
     def close(self):
         if self.pg:
@@ -217,7 +219,21 @@ def time_steps(dist, step, steps: int, warmup: int):
     return dist.max(ms), launches, per_kernel
 
 
-def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None, workload=""):
+def tensor_peak(pk, clocks):
+    """(peak TFLOP/s, label) for a tensor-bound kernel: the burst figure
+    (cuBLAS bf16 at full clock) while the SM clock sampled during the timed
+    region stays within 10 % of its maximum, else the sustained one."""
+    if clocks and clocks.get("sm_max_mhz") and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"]:
+        return pk["bf16_tflops_sustained"], "sustained"
+    return pk["bf16_tflops"], "burst"
+
+
+def roofline(per_kernel, flops_fwd, pk, peak_src, clocks=None, kv_bytes=None, workload="",
+             scale_units=1.0):
+    """Roofline of the dominant kernel.  flops_fwd / kv_bytes are this
+    rank's algorithmic work per step; `traffic` is the committed ncu DRAM
+    byte count of one full-size launch scaled by this rank's share of the
+    (batch, head) units."""
     if not per_kernel:
         return None
     name, (tot, cnt) = max(per_kernel.items(), key=lambda kv: kv[1][0])
@@ -225,11 +241,11 @@ def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None, work
     avg_s = tot / cnt / 1e3
     if kind == "decode":
         achieved = kv_bytes / avg_s / 1e9   # one split launch reads every visible K/V row once
-        peak = pk["hbm_gbs"]
+        peak, which = pk["hbm_gbs"], "HBM copy"
         unit, bound = "GB/s", "hbm"
     elif kind in KERNEL_WORK:
         achieved = KERNEL_WORK[kind] * flops_fwd / avg_s / 1e12
-        peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+        peak, which = tensor_peak(pk, clocks)
         unit, bound = "TFLOP/s", "tensor"
     else:
         return None
@@ -237,26 +253,45 @@ def roofline(per_kernel, flops_fwd, pk, peak_src, sustained, kv_bytes=None, work
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as fh:
-            traffic = json.load(fh).get(f"{name}@{workload}")
+            t = json.load(fh).get(f"{name}@{workload}")
+        traffic = None if t is None else int(round(t * scale_units))
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
             "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
-            "peak_source": f"{peak_src} ({'sustained' if sustained and bound == 'tensor' else 'burst'})",
+            "peak_source": f"{peak_src} ({which})",
             "avg_launch_ms": round(tot / cnt, 4), "launches": cnt,
             "kernel_share": {k: round(v[0] / sum(x[0] for x in per_kernel.values()), 4)
                              for k, v in per_kernel.items()}}
 
 
-def make_inputs(cfg, rank: int, n_q=None):
+def executed_mma_flops(mask, cfg, units):
+    """Tensor-core FLOPs each kernel issues per step for `units` (batch,
+    head) pairs, from the kept tiles of the plans the kernels walk (the
+    forward's 256-row query-pair tiles visit the union of both tiles' kept
+    key tiles; the dQ kernel recomputes S and dP), next to the algorithmic
+    FLOPs of the same launch."""
+    import sparse_triton_kernel as stk
+    D, N, dt = cfg["D"], cfg["N"], cfg["dtype"]
+    out = {}
+    for kind, pass_id, gemms in (("fwd", 0, 2), ("dkdv", 2, 4), ("dq", 1, 3)):
+        p = stk._plan_for(mask, pass_id, dt, D, N, N, cfg["BM"], cfg["BN"])
+        tm, tn = p["tiles"]
+        tiles = int(p["nnz"].item())
+        out[kind] = gemms * 2.0 * tm * tn * D * tiles * units
+    return out
+
+
+def make_inputs(cfg, seed: int, n_q=None, local=None):
+    """Seeded N(0,1) Q, K, V of a configuration (x0.5 for config 3); with
+    `local` = (start, stop) only that range of the (batch, head) units, as a
+    [1, stop - start, N, D] tensor."""
     dev = torch.device("cuda")
-    g = torch.Generator(device=dev).manual_seed(rank)
+    g = torch.Generator(device=dev).manual_seed(seed)
     mul = 0.5 if cfg is CFG3 else 1.0
     nq = cfg["N"] if n_q is None else n_q
-    q = torch.randn(cfg["B"], cfg["H"], nq, cfg["D"], generator=g, device=dev,
-                    dtype=cfg["dtype"])
-    k = torch.randn(cfg["B"], cfg["H"], cfg["N"], cfg["D"], generator=g, device=dev,
-                    dtype=cfg["dtype"])
-    v = torch.randn(cfg["B"], cfg["H"], cfg["N"], cfg["D"], generator=g, device=dev,
-                    dtype=cfg["dtype"])
+    B, H = (cfg["B"], cfg["H"]) if local is None else (1, local[1] - local[0])
+    q = torch.randn(B, H, nq, cfg["D"], generator=g, device=dev, dtype=cfg["dtype"])
+    k = torch.randn(B, H, cfg["N"], cfg["D"], generator=g, device=dev, dtype=cfg["dtype"])
+    v = torch.randn(B, H, cfg["N"], cfg["D"], generator=g, device=dev, dtype=cfg["dtype"])
     if mul != 1.0:
         for t in (q, k, v):
             t.mul_(mul)
@@ -319,14 +354,55 @@ def e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, steps: int, warmu
     return dist.max(start.elapsed_time(end))
 
 
+def local_units(dist, cfg):
+    """This rank's contiguous share [start, stop) of the B*H (batch, head)
+    units of a configuration (the whole range on one GPU)."""
+    import shard
+    return shard.shard_units(cfg["B"] * cfg["H"], dist.world, dist.rank)
+
+
+def gather_units(dist, t, start, stop, units):
+    """All ranks' [1, n, ...] slices of a (batch, head)-sharded tensor,
+    reassembled on every rank as [units, ...] (NCCL all_gather; shards are
+    padded to the largest one)."""
+    import shard
+    sizes = [b - a for a, b in (shard.shard_units(units, dist.world, r)
+                                for r in range(dist.world))]
+    cap = max(sizes)
+    flat = t.reshape(stop - start, *t.shape[2:])
+    if dist.world == 1:
+        return flat
+    import torch.distributed as tdist
+    pad = torch.zeros((cap,) + tuple(flat.shape[1:]), dtype=flat.dtype, device=flat.device)
+    pad[: stop - start] = flat
+    out = torch.empty((dist.world * cap,) + tuple(flat.shape[1:]), dtype=flat.dtype,
+                      device=flat.device)
+    tdist.all_gather_into_tensor(out, pad)
+    return torch.cat([out[r * cap: r * cap + n] for r, n in enumerate(sizes)])
+
+
 def bench_fwdbwd(dist, args, pk, src):
+    """Config 2 fwd+bwd.  The global problem is fixed (B=4, H=32: 128
+    (batch, head) units); each rank takes a contiguous share of the units
+    (strong scaling) and reads it as a [1, units, N, D] view, with no
+    collective on the data path.  After the timed region every rank's O, dQ,
+    dK, dV are all-gathered (NCCL) and rank 0 compares them bit for bit with
+    its own single-GPU run of the whole problem on the same inputs."""
+    import shard
     import sparse_triton_kernel as stk
     cfg = CFG2
     nnz, mask = kept_blocks(cfg)
-    F = f_fwd(cfg, nnz)
-    q, k, v = make_inputs(cfg, dist.rank)
-    g1 = torch.Generator(device="cuda").manual_seed(1000 + dist.rank)
-    do = torch.randn(q.shape, generator=g1, device="cuda", dtype=cfg["dtype"])
+    F = f_fwd(cfg, nnz)                       # the whole problem
+    units = cfg["B"] * cfg["H"]
+    start, stop = local_units(dist, cfg)
+    F_local = F * (stop - start) / units
+    q_full, k_full, v_full = make_inputs(cfg, 0)
+    g1 = torch.Generator(device="cuda").manual_seed(1)
+    do_full = torch.randn(q_full.shape, generator=g1, device="cuda", dtype=cfg["dtype"])
+    q, k, v, do = (shard.bh_slice(t, start, stop).clone()
+                   for t in (q_full, k_full, v_full, do_full))
+    if dist.rank != 0:
+        del q_full, k_full, v_full, do_full
     for t in (q, k, v):
         t.requires_grad_(True)
     kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
@@ -343,13 +419,27 @@ def bench_fwdbwd(dist, args, pk, src):
     clocks.start()
     ms, launches, per_kernel = time_steps(dist, step, args.steps, args.warmup)
     clk = clocks.stop()
+    value = 3.5 * F * args.steps / (ms / 1e3) / 1e12
+
+    # verification (outside the timed region)
     o = step()
     torch.cuda.synchronize()
-    sums = dist.gather_checksums([float(o.detach().double().sum()),
-                                  float(q.grad.double().abs().sum())])
-    finite = all(math.isfinite(x) for r in sums for x in r)
-    total_flops = 3.5 * F * dist.world * args.steps
-    value = total_flops / (ms / 1e3) / 1e12
+    got = [gather_units(dist, x.detach(), start, stop, units)
+           for x in (o, q.grad, k.grad, v.grad)]
+    verify = None
+    if dist.rank == 0:
+        qf, kf, vf = (t.clone().requires_grad_(True) for t in (q_full, k_full, v_full))
+        of = stk.block_sparse_attention(qf, kf, vf, mask, **kw)
+        of.backward(do_full)
+        ref = [x.detach().reshape(units, *x.shape[2:]) for x in (of, qf.grad, kf.grad, vf.grad)]
+        same = [bool(torch.equal(a, b)) for a, b in zip(got, ref)]
+        finite = all(bool(torch.isfinite(a).all()) for a in got)
+        verify = {"gathered": "O, dQ, dK, dV of all ranks (NCCL all_gather)" if dist.world > 1
+                  else "O, dQ, dK, dV (one rank)",
+                  "bitwise_equal_to_1gpu_run": dict(zip(("o", "dq", "dk", "dv"), same)),
+                  "finite": finite}
+        del qf, kf, vf, of, ref, q_full, k_full, v_full, do_full
+    del got
 
     # e2e through the public API from pinned host memory: every step copies its
     # inputs (Q, K, V, dO) host->device and its results (O, dQ, dK, dV)
@@ -368,25 +458,62 @@ def bench_fwdbwd(dist, args, pk, src):
     bytes_h2d = sum(t.numel() * t.element_size() for t in host_in)
     bytes_d2h = sum(t.numel() * t.element_size() for t in out_h[0])
     e2e = None if args.no_e2e else {
-        "value": round(3.5 * F * dist.world * e_steps / (e_ms / 1e3) / 1e12, 3),
-        "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d, "d2h_bytes_per_step": bytes_d2h,
+        "value": round(3.5 * F * e_steps / (e_ms / 1e3) / 1e12, 3),
+        "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d * dist.world,
+        "d2h_bytes_per_step": bytes_d2h * dist.world,
         "ms_per_step": round(e_ms / e_steps, 3),
         "pipeline": "copy-in / compute / copy-out on three streams, two steps in flight"}
-    del dev_in
-    rl = roofline(per_kernel, F, pk, src, sustained=True, workload="cfg2")
+    del dev_in, hq, hk, hv, hdo, host_in, out_h
+    rl = roofline(per_kernel, F_local, pk, src, clocks=clk, workload="cfg2",
+                  scale_units=(stop - start) / units)
     res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
-               nnz=nnz, flops_fwd=F, finite=finite, per_kernel=per_kernel)
-    del q, k, v, do, hq, hk, hv, hdo, host_in, out_h
+               nnz=nnz, flops_fwd=F, verify=verify, per_kernel=per_kernel,
+               units=(start, stop, units))
+    del q, k, v, do
     torch.cuda.empty_cache()
+    if dist.world > 1 and not args.no_weak:
+        res["weak"] = bench_fwdbwd_weak(dist, args, F)
     return res
 
 
+def bench_fwdbwd_weak(dist, args, F):
+    """Weak scaling for reference: every rank runs the whole config-2 batch
+    (the job's batch is 4 * N); value = all ranks' FLOPs / max time."""
+    import sparse_triton_kernel as stk
+    cfg = CFG2
+    _, mask = kept_blocks(cfg)
+    q, k, v = make_inputs(cfg, dist.rank)
+    g1 = torch.Generator(device="cuda").manual_seed(1000 + dist.rank)
+    do = torch.randn(q.shape, generator=g1, device="cuda", dtype=cfg["dtype"])
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
+              window_size=cfg["W"])
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        stk.block_sparse_attention(q, k, v, mask, **kw).backward(do)
+
+    steps = max(2, min(args.steps, 5))
+    ms, _, _ = time_steps(dist, step, steps, args.warmup)
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    return {"value": round(3.5 * F * dist.world * steps / (ms / 1e3) / 1e12, 3),
+            "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 3), "global_batch": 4 * dist.world,
+            "scaling": "weak"}
+
+
 def bench_fwd(dist, args, pk, src):
+    """Config 3 prefill forward; the 32 (batch, head) units are split across
+    ranks like config 2's."""
     import sparse_triton_kernel as stk
     cfg = CFG3
     nnz, mask = kept_blocks(cfg)
     F = f_fwd(cfg, nnz)
-    q, k, v = make_inputs(cfg, dist.rank)
+    start, stop = local_units(dist, cfg)
+    units = cfg["B"] * cfg["H"]
+    q, k, v = make_inputs(cfg, dist.rank, local=(start, stop))
     kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
               window_size=cfg["W"])
 
@@ -394,24 +521,44 @@ def bench_fwd(dist, args, pk, src):
         with torch.no_grad():
             return stk.block_sparse_attention(q, k, v, mask, **kw)
 
-    ms, launches, per_kernel = time_steps(dist, step, max(2, args.steps), args.warmup)
-    value = F * dist.world * max(2, args.steps) / (ms / 1e3) / 1e12
-    rl = roofline(per_kernel, F, pk, src, sustained=False, workload="cfg3")
+    steps = max(2, args.steps)
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
+    clk = clocks.stop()
+    value = F * steps / (ms / 1e3) / 1e12
+    share = (stop - start) / units
+    rl = roofline(per_kernel, F * share, pk, src, clocks=clk, workload="cfg3", scale_units=share)
     del q, k, v
     torch.cuda.empty_cache()
-    return dict(value=value, ms=ms / max(2, args.steps), roofline=rl, nnz=nnz, launches=launches)
+    return dict(value=value, ms=ms / steps, roofline=rl, nnz=nnz, launches=launches, clocks=clk,
+                units=(start, stop, units))
 
 
 def bench_decode(dist, args, pk, src):
+    """Config 4 decode over a full 100001-token cache, then over a
+    StreamingLLM ring cache; the 2048 (batch, head) units are split across
+    ranks."""
     import sparse_triton_kernel as stk
     cfg = CFG4
     _, mask = kept_blocks(cfg)
-    # the ring cache of the second measurement is allocated before the 105 GB
-    # full cache, on an empty device (as a serving process would hold it)
+    start, stop = local_units(dist, cfg)
+    units = cfg["B"] * cfg["H"]
+    share = (stop - start) / units
+    # the ring cache of the second measurement is allocated before the full
+    # cache, on an empty device (as a serving process would hold it)
     from streaming_kv_cache import StreamingKVCache
-    cache = StreamingKVCache(cfg["B"], cfg["H"], cfg["D"], cfg["S"], cfg["W"], dtype=cfg["dtype"])
-    q, k, v = make_inputs(cfg, dist.rank, n_q=1)
-    kv_bytes, qo_bytes = decode_bytes(cfg)
+    cache = StreamingKVCache(1, stop - start, cfg["D"], cfg["S"], cfg["W"], dtype=cfg["dtype"])
+    # grouped-query variant: the same query heads over GQA_GROUP times fewer
+    # K/V heads (allocated up front too, before the full cache)
+    n_loc = stop - start
+    gq = GQA_GROUP if n_loc % GQA_GROUP == 0 else 1
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    k_g = torch.randn(1, n_loc // gq, cfg["N"], cfg["D"], generator=gen, device="cuda",
+                      dtype=cfg["dtype"])
+    v_g = torch.randn_like(k_g)
+    q, k, v = make_inputs(cfg, dist.rank, n_q=1, local=(start, stop))
+    kv_bytes, qo_bytes = decode_bytes(cfg)        # the whole problem
     kw = dict(block_m=cfg["BM"], block_n=cfg["BN"], is_causal=True, sink_size=cfg["S"],
               window_size=cfg["W"])
 
@@ -421,8 +568,9 @@ def bench_decode(dist, args, pk, src):
 
     steps = max(5, args.steps * 5)
     ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
-    value = kv_bytes * dist.world * steps / (ms / 1e3) / 1e9
-    rl = roofline(per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes, workload="cfg4")
+    value = kv_bytes * steps / (ms / 1e3) / 1e9
+    rl = roofline(per_kernel, 0.0, pk, src, kv_bytes=kv_bytes * share, workload="cfg4",
+                  scale_units=share)
 
     # the same decode over a StreamingLLM ring cache holding sink + window rows
     # (timed before the full cache is freed: a large free is followed by the
@@ -434,17 +582,33 @@ def bench_decode(dist, args, pk, src):
         return cache.attend(q)
 
     r_ms, r_launches, r_per_kernel = time_steps(dist, ring_step, steps, args.warmup)
-    ring = {"value": round(kv_bytes * dist.world * steps / (r_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+
+    def gqa_step():
+        with torch.no_grad():
+            return stk.block_sparse_attention(q, k_g, v_g, mask, **kw)
+
+    g_ms, g_launches, g_per_kernel = time_steps(dist, gqa_step, steps, args.warmup)
+    g_bytes = kv_bytes / gq        # each K/V head's visible rows, read once for its group
+    gqa = {"value": round(g_bytes * steps / (g_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(g_ms / steps, 4), "kv_heads_per_query_heads": f"1/{gq}",
+           "kv_bytes_per_step": int(g_bytes),
+           "roofline": roofline(g_per_kernel, 0.0, pk, src, kv_bytes=g_bytes * share,
+                                workload=f"cfg4_gqa{gq}", scale_units=share),
+           "gpu_launches": g_launches,
+           "config": f"config 4 geometry with {CFG4['H'] // gq} K/V heads for {CFG4['H']} "
+                     "query heads (grouped-query attention)"}
+    del k_g, v_g
+    ring = {"value": round(kv_bytes * steps / (r_ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "ms_per_step": round(r_ms / steps, 4), "cache_bytes": cache.memory_bytes,
             "full_cache_bytes": full_bytes,
             "memory_ratio": round(full_bytes / cache.memory_bytes, 2),
-            "roofline": roofline(r_per_kernel, 0.0, pk, src, sustained=False, kv_bytes=kv_bytes,
-                                 workload="cfg4_ring"),
+            "roofline": roofline(r_per_kernel, 0.0, pk, src, kv_bytes=kv_bytes * share,
+                                 workload="cfg4_ring", scale_units=share),
             "gpu_launches": r_launches}
     del q, k, v, cache
     torch.cuda.empty_cache()
     return dict(value=value, ms=ms / steps, roofline=rl, kv_bytes=kv_bytes, qo_bytes=qo_bytes,
-                launches=launches, ring=ring)
+                launches=launches, ring=ring, gqa=gqa, units=(start, stop, units))
 
 
 def bench_fx(dist, args, pk, src):
@@ -556,15 +720,18 @@ def cpu_baseline_fwdbwd(budget_s: float = 20.0):
 
 
 def base_line(args, world):
+    units = CFG2["B"] * CFG2["H"]
     return {"metric": "kept-block attn TFLOP/s fwd+bwd", "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v/dO, BASELINE config 2 shapes)",
             "config": {"workload": "cfg2 sparse prefill fwd+bwd: B=4 H=32 N=16384 D=128 bf16 "
-                                   "S=4 W=2048 BM=BN=128 per rank",
-                       "global_batch": 4 * world, "seq_len": 16384, "heads": CFG2["H"],
-                       "head_dim": 128, "parallelism": f"(batch,head) shards x{world}",
-                       "l2": "inputs exceed L2 (537 MB per tensor); no flush"}}
+                                   "S=4 W=2048 BM=BN=128 (whole problem, split across GPUs)",
+                       "global_batch": CFG2["B"], "seq_len": 16384, "heads": CFG2["H"],
+                       "head_dim": 128,
+                       "parallelism": f"(batch,head) shards: {units} units over {world} GPU(s)",
+                       "l2": "inputs exceed L2 (537 MB per tensor at 1 GPU; "
+                             f"{537 // world} MB per GPU at {world}); no flush"}}
 
 
 def run_reference(args):
@@ -598,8 +765,12 @@ def main():
                     help="override the layer count of the config-5 model (small runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
-                    help="override the per-rank head count (small cases for profiling)")
+                    help="override the head count of configs 2-4 (small cases for profiling)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="skip the weak-scaling reference leg (N > 1)")
+    ap.add_argument("--no-fx", action="store_true",
+                    help="skip the config-5 FX end-to-end leg of the default run")
     args = ap.parse_args()
     if args.heads > 0:
         for cfg in (CFG2, CFG3, CFG4):
@@ -621,14 +792,25 @@ def main():
         line.update({"value": round(r["value"], 3), "ms_per_step": round(r["ms"] / args.steps, 3),
                      "e2e": r["e2e"], "roofline": r["roofline"], "clocks": r["clocks"],
                      "gpu_launches": r["launches"]})
+        start, stop, units = r["units"]
         extra["fwdbwd"] = {"kept_blocks": r["nnz"], "flops_fwd": r["flops_fwd"],
-                           "outputs_finite_all_ranks": r["finite"],
+                           "units_rank0": [start, stop], "units_total": units,
+                           "verify_rank0": r["verify"],
                            "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()}}
+        _, mask = kept_blocks(CFG2)
+        ex = executed_mma_flops(mask, CFG2, stop - start)
+        alg = {k: KERNEL_WORK[k] * r["flops_fwd"] * (stop - start) / units for k in ex}
+        extra["fwdbwd"]["mma_flops_per_launch_rank0"] = {
+            k: {"executed": ex[k], "algorithmic": alg[k], "ratio": round(ex[k] / alg[k], 4)}
+            for k in ex}
+        if "weak" in r:
+            extra["fwdbwd_weak_scaling"] = r["weak"]
     if args.workload in ("all", "fwd"):
         r = bench_fwd(dist, args, pk, src)
         extra["cfg3_prefill_fwd"] = {"value": round(r["value"], 3), "unit": "TFLOP/s",
                                      "ms_per_step": round(r["ms"], 3), "roofline": r["roofline"],
-                                     "kept_blocks": r["nnz"], "gpu_launches": r["launches"]}
+                                     "kept_blocks": r["nnz"], "gpu_launches": r["launches"],
+                                     "clocks": r["clocks"], "units_rank0": list(r["units"][:2])}
         if args.workload == "fwd":
             line.update({"metric": "kept-block attn TFLOP/s fwd", "value": extra[
                 "cfg3_prefill_fwd"]["value"], "roofline": r["roofline"], "dtype": "fp16"})
@@ -637,19 +819,21 @@ def main():
         extra["cfg4_decode"] = {"value": round(r["value"], 2), "unit": "GB/s",
                                 "ms_per_step": round(r["ms"], 4), "roofline": r["roofline"],
                                 "kv_bytes_per_step": r["kv_bytes"],
-                                "gpu_launches": r["launches"]}
+                                "gpu_launches": r["launches"], "units_rank0": list(r["units"][:2])}
         extra["cfg4_decode_ring_cache"] = r["ring"]
+        extra["cfg4_decode_gqa"] = r["gqa"]
         if args.workload == "decode":
             line.update({"metric": "decode KV GB/s", "unit": "GB/s", "value": extra[
                 "cfg4_decode"]["value"], "roofline": r["roofline"], "dtype": "fp16"})
-    if args.workload == "fx":
+    if args.workload == "fx" or (args.workload == "all" and dist.world == 1 and not args.no_fx):
         r = bench_fx(dist, args, pk, src)
         extra["cfg5_fx_end_to_end"] = r
-        line.update({"metric": "FX end-to-end tokens/s (fwd+bwd)", "unit": "tokens/s",
-                     "value": r["tokens_per_s"], "ms_per_step": r["ms_per_step"],
-                     "gpu_launches": r["gpu_launches"], "config": {
-                         "workload": r["config"], "global_batch": CFG5["B"] * dist.world,
-                         "seq_len": CFG5["N"], "parallelism": f"replicas x{dist.world}"}})
+        if args.workload == "fx":
+            line.update({"metric": "FX end-to-end tokens/s (fwd+bwd)", "unit": "tokens/s",
+                         "value": r["tokens_per_s"], "ms_per_step": r["ms_per_step"],
+                         "gpu_launches": r["gpu_launches"], "scaling": "weak", "config": {
+                             "workload": r["config"], "global_batch": CFG5["B"] * dist.world,
+                             "seq_len": CFG5["N"], "parallelism": f"replicas x{dist.world}"}})
     line["extra"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and \
             args.workload in ("all", "fwdbwd"):

@@ -30,9 +30,10 @@ int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t wind
 int decode_group(int dtype, int64_t D);
 int decode_nsplit(int64_t BH, int64_t est_tiles);
 int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit);
+int decode_heads_per_cta(int group);
 int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
-               const int32_t* ci, int nsplit, cudaStream_t s);
+               const int32_t* ci, int nsplit, int heads, int group, cudaStream_t s);
 // attn_tc.cu
 bool tc_supports(int pass, int dtype, int64_t D);
 int tc_tiles(int pass, int64_t* tm, int64_t* tn);
@@ -103,6 +104,22 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+int device_sm_count() {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int n = 0;
+    cached[dev] =
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0
+            ? n
+            : 148;
+  }
+  return cached[dev];
+}
 
 int* device_status_ptr() {
   int dev = 0;
@@ -206,7 +223,7 @@ int check_tma(const void* const* ptrs, const Strides3* const* st, int count, con
 
 using namespace sbfa;
 
-extern "C" int sbfa_abi_version(void) { return 3; }
+extern "C" int sbfa_abi_version(void) { return 4; }
 
 extern "C" int64_t sbfa_launch_count(void) { return g_launches.load(); }
 
@@ -362,11 +379,40 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
 }
 
 
+namespace sbfa {
+// Every check sbfa_decode makes on its tensors and shape, before anything is
+// launched (shared with sbfa_decode_noalloc, which builds its plan only once
+// these pass).
+int check_decode_args(const void* q, const void* k, const void* v, const void* o, int64_t B,
+                      int64_t H, int64_t n_kv, int64_t head_dim, int dtype, int64_t sink,
+                      int64_t window, const int32_t* block_mask, int64_t block_m,
+                      int64_t block_n, int64_t kv_heads) {
+  if (int rc = check_common(B, H, 1, n_kv, head_dim, dtype, sink, window, block_mask, block_m,
+                            block_n))
+    return rc;
+  if (!q || !k || !v || !o) return fail(SBFA_ERR_INVALID, "decode: NULL tensor pointer");
+  if (kv_heads > 0 && (kv_heads > H || H % kv_heads != 0))
+    return fail(SBFA_ERR_INVALID, "the query head count must be a multiple of kv_heads");
+  if (decode_group(dtype, head_dim) == 0)
+    return fail(SBFA_ERR_UNSUPPORTED,
+                "decode: head_dim * element size must be 16..512 bytes in powers of two "
+                "(fp16/bf16/fp32)");
+  for (const void* p : {q, k, v, o})
+    if (((uintptr_t)p & 15u) != 0)
+      return fail(SBFA_ERR_UNSUPPORTED, "decode: tensors must be 16-byte aligned");
+  return SBFA_OK;
+}
+}  // namespace sbfa
+
 extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
                                                int64_t head_dim, int64_t block_n) {
   (void)block_n;
   // sized for the worst case over masks (non-causal: every tile may be kept)
-  const int ns = decode_nsplit(B * H, decode_est_tiles(n_kv, 0, 0, 0));
+  // and over head groupings (the most query heads per CTA, so the fewest
+  // CTAs per split and the most splits)
+  if (B <= 0 || H <= 0 || head_dim <= 0 || n_kv <= 0) return 0;
+  const int64_t ctas = std::max<int64_t>(1, B * H / decode_heads_per_cta(1 << 30));
+  const int ns = decode_nsplit(ctas, decode_est_tiles(n_kv, 0, 0, 0));
   return decode_ws_bytes(B * H, head_dim, ns);
 }
 
@@ -375,27 +421,23 @@ extern "C" int sbfa_decode(const void* q, const void* k, const void* v, void* o,
                            double softmax_scale, int is_causal, int64_t sink, int64_t window,
                            const int32_t* block_mask, int64_t block_m, int64_t block_n,
                            const int32_t* row_ptr, const int32_t* col_idx, void* split_ws,
-                           int64_t split_ws_bytes, void* stream) {
-  if (int rc = check_common(B, H, 1, n_kv, head_dim, dtype, sink, window, block_mask, block_m,
-                            block_n))
+                           int64_t split_ws_bytes, int64_t kv_heads, void* stream) {
+  if (int rc = check_decode_args(q, k, v, o, B, H, n_kv, head_dim, dtype, sink, window,
+                                 block_mask, block_m, block_n, kv_heads))
     return rc;
-  if (!q || !k || !v || !o || !row_ptr || !col_idx)
-    return fail(SBFA_ERR_INVALID, "sbfa_decode: NULL tensor or plan pointer");
-  if (decode_group(dtype, head_dim) == 0)
-    return fail(SBFA_ERR_UNSUPPORTED,
-                "sbfa_decode: head_dim * element size must be 16..512 bytes in powers of two "
-                "(fp16/bf16/fp32)");
-  for (const void* p : {q, k, v, (const void*)o})
-    if (((uintptr_t)p & 15u) != 0)
-      return fail(SBFA_ERR_UNSUPPORTED, "sbfa_decode: tensors must be 16-byte aligned");
-  const int ns = decode_nsplit(B * H, decode_est_tiles(n_kv, is_causal, sink, window));
+  if (!row_ptr || !col_idx) return fail(SBFA_ERR_INVALID, "sbfa_decode: NULL plan pointer");
+  if (kv_heads <= 0) kv_heads = H;
+  const int group = (int)(H / kv_heads);
+  const int ns = decode_nsplit(B * H / decode_heads_per_cta(group),
+                               decode_est_tiles(n_kv, is_causal, sink, window));
   const int64_t need = decode_ws_bytes(B * H, head_dim, ns);
   if (need > 0 && (split_ws == nullptr || split_ws_bytes < need))
     return fail(SBFA_ERR_INVALID, "sbfa_decode: split workspace too small (need " +
                                       std::to_string(need) + " bytes)");
   MaskParams mp = make_mp(1, n_kv, is_causal, sink, window, block_mask, block_m, block_n);
   return decode_run(dtype, q, k, v, o, lse, split_ws, (int)(B * H), (int)head_dim,
-                    softmax_scale, mp, row_ptr, col_idx, ns, (cudaStream_t)stream);
+                    softmax_scale, mp, row_ptr, col_idx, ns, (int)H, group,
+                    (cudaStream_t)stream);
 }
 
 extern "C" int sbfa_decode_supported(int dtype, int64_t head_dim) {

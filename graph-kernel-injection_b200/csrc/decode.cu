@@ -12,6 +12,8 @@
 //  * each key row is read by a group of G lanes with 16-byte loads
 //    (G = D * sizeof(T) / 16; 16 lanes for D = 128 fp16), fully coalesced,
 //    U keys in flight per group;
+//  * with grouped-query attention a CTA serves up to 4 query heads of one
+//    key/value head, so each K/V row is read once for all of them;
 //  * every CTA keeps an online-softmax partial (m, l, acc[D]) per lane group,
 //    merges its groups through shared memory and either writes O / LSE
 //    directly (one split) or a partial to the workspace, merged by
@@ -24,12 +26,16 @@
 namespace sbfa {
 
 int decode_group(int dtype, int64_t D);
+int decode_heads_per_cta(int group);
+int check_decode_args(const void* q, const void* k, const void* v, const void* o, int64_t B,
+                      int64_t H, int64_t n_kv, int64_t head_dim, int dtype, int64_t sink,
+                      int64_t window, const int32_t* block_mask, int64_t block_m,
+                      int64_t block_n, int64_t kv_heads);
 
 namespace {
 
 constexpr int kDecThreads = 128;
 constexpr int kDecTile = 64;   // keys per plan tile (pass 3)
-constexpr int kUnroll = 4;     // keys in flight per lane group
 
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& w, float* f) {
@@ -82,53 +88,73 @@ struct RingKeys {
   }
 };
 
-// Partial record layout in the workspace: [m, l, acc[0..D)] floats.
-template <typename T, int G, typename Keys>
+// Partial record layout in the workspace: [m, l, acc[0..D)] floats, one per
+// (query (batch, head), split).
+//
+// A CTA serves QG query heads that share one key/value head (grouped-query
+// attention: query head h reads key/value head h / group; QG divides the
+// group, QG = group = 1 without grouping), so every K/V row it loads is
+// used by all QG queries.  Lane l of a G-lane group holds elements
+// [l*EPV, (l+1)*EPV) of the row for every one of the QG queries; dot
+// products and accumulators use packed fp32x2 FMAs.
+template <typename T, int G, int QG, int U, typename Keys>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     T* __restrict__ o, float* __restrict__ lse, float* __restrict__ ws, int D, float scale,
-    Keys keys, int64_t kv_rows, int nsplit) {
+    Keys keys, int64_t kv_rows, int nsplit, int heads, int group) {
   constexpr int EPV = 16 / sizeof(T);      // elements per 16-byte vector
+  constexpr int E2 = EPV / 2;              // fp32 pairs per vector
   constexpr int GPW = 32 / G;              // lane groups per warp
   constexpr int NG = (kDecThreads / 32) * GPW;
-  __shared__ float sm_m[NG], sm_l[NG];
-  extern __shared__ float sm_acc[];        // [NG][D]
+  __shared__ float sm_m[QG][NG], sm_l[QG][NG];
+  extern __shared__ float sm_acc[];        // [QG][NG][D]
 
   const int split = blockIdx.x;
-  const size_t bh = blockIdx.y;
+  const size_t bh0 = (size_t)blockIdx.y * QG;   // first query (batch, head) of the CTA
+  const size_t kvh = (bh0 / heads) * (size_t)(heads / group) + (bh0 % heads) / group;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = lane / G, gl = lane % G;
   const int gid = warp * GPW + grp;
 
-  // query slice of this lane, pre-scaled
-  float qv[EPV];
-  {
-    const uint4 w = __ldg(reinterpret_cast<const uint4*>(q + bh * (size_t)D) + gl);
-    unpack16<T>(w, qv);
+  // query slices of this lane, pre-scaled
+  float2 qv[QG][E2];
 #pragma unroll
-    for (int i = 0; i < EPV; ++i) qv[i] *= scale;
+  for (int j = 0; j < QG; ++j) {
+    float f[EPV];
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(q + (bh0 + j) * (size_t)D) + gl);
+    unpack16<T>(w, f);
+#pragma unroll
+    for (int i = 0; i < E2; ++i) qv[j][i] = make_float2(f[2 * i] * scale, f[2 * i + 1] * scale);
   }
   // this split's candidates: [t_lo, t_hi), in whole 64-key tiles
   const int all = keys.total();
   const int per = ((all + nsplit - 1) / nsplit + kDecTile - 1) / kDecTile * kDecTile;
   const int t_lo = split * per;
   const int total = max(0, min(all, t_lo + per) - t_lo);
-  const uint4* kb = reinterpret_cast<const uint4*>(k + bh * (size_t)kv_rows * D);
-  const uint4* vb = reinterpret_cast<const uint4*>(v + bh * (size_t)kv_rows * D);
+  const uint4* kb = reinterpret_cast<const uint4*>(k + kvh * (size_t)kv_rows * D);
+  const uint4* vb = reinterpret_cast<const uint4*>(v + kvh * (size_t)kv_rows * D);
   const int vec_per_row = D / EPV;   // == G
 
-  float m = -INFINITY, l = 0.f, acc[EPV];
+  float m[QG], l[QG];
+  float2 acc[QG][E2];
 #pragma unroll
-  for (int i = 0; i < EPV; ++i) acc[i] = 0.f;
+  for (int j = 0; j < QG; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < E2; ++i) acc[j][i] = make_float2(0.f, 0.f);
+  }
 
-  const int step = NG * kUnroll;
+  const int step = NG * U;
   for (int base = 0; base < total; base += step) {
-    uint4 kw[kUnroll], vw[kUnroll];
-    bool vis[kUnroll];
+    uint4 kw[U], vw[U];
+    bool vis[U];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int t = base + u * NG + gid;
       vis[u] = false;
+      kw[u] = make_uint4(0u, 0u, 0u, 0u);
+      vw[u] = kw[u];
       if (t < total) {
         int key = 0;
         vis[u] = keys.key(t_lo + t, &key);
@@ -138,74 +164,87 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
         }
       }
     }
-    float s[kUnroll];
-    float tile_max = -INFINITY;
+    float s[U][QG];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       float kf[EPV];
-      float d = 0.f;
-      if (vis[u]) {
-        unpack16<T>(kw[u], kf);
+      unpack16<T>(kw[u], kf);
 #pragma unroll
-        for (int i = 0; i < EPV; ++i) d += qv[i] * kf[i];
+      for (int j = 0; j < QG; ++j) {
+        float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < E2; ++i) d2 = __ffma2_rn(qv[j][i], make_float2(kf[2 * i], kf[2 * i + 1]), d2);
+        float d = d2.x + d2.y;
+#pragma unroll
+        for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+        s[u][j] = vis[u] ? d : -INFINITY;
       }
-#pragma unroll
-      for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-      s[u] = vis[u] ? d : -INFINITY;
-      tile_max = fmaxf(tile_max, s[u]);
     }
-    // No shuffles below this point in the iteration, so the per-group
-    // branch cannot split a warp-collective.
-    const float m_new = fmaxf(m, tile_max);
-    if (m_new != -INFINITY) {
-      const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
-      l *= alpha;
+    // No shuffles below this point in the iteration.  A query whose keys so
+    // far are all invisible keeps m = -inf; the exponents then use 0 as
+    // their reference so that no -inf - -inf appears (every p is 0).
+    float mref[QG];
 #pragma unroll
-      for (int i = 0; i < EPV; ++i) acc[i] *= alpha;
+    for (int j = 0; j < QG; ++j) {
+      float tmax = s[0][j];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (!vis[u]) continue;
-        const float p = __expf(s[u] - m_new);
-        l += p;
-        float vf[EPV];
-        unpack16<T>(vw[u], vf);
+      for (int u = 1; u < U; ++u) tmax = fmaxf(tmax, s[u][j]);
+      const float m_new = fmaxf(m[j], tmax);
+      mref[j] = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = __expf(m[j] - mref[j]);
+      l[j] *= alpha;
 #pragma unroll
-        for (int i = 0; i < EPV; ++i) acc[i] += p * vf[i];
+      for (int i = 0; i < E2; ++i) acc[j][i] = __fmul2_rn(acc[j][i], make_float2(alpha, alpha));
+      m[j] = m_new;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!vis[u]) continue;
+      float vf[EPV];
+      unpack16<T>(vw[u], vf);
+#pragma unroll
+      for (int j = 0; j < QG; ++j) {
+        const float p = __expf(s[u][j] - mref[j]);
+        l[j] += p;
+#pragma unroll
+        for (int i = 0; i < E2; ++i)
+          acc[j][i] = __ffma2_rn(make_float2(p, p), make_float2(vf[2 * i], vf[2 * i + 1]), acc[j][i]);
       }
-      m = m_new;
     }
   }
 
-  // merge lane groups of the CTA
-  if (gl == 0) { sm_m[gid] = m; sm_l[gid] = l; }
+  // merge the lane groups of the CTA, per query
 #pragma unroll
-  for (int i = 0; i < EPV; ++i) sm_acc[gid * D + gl * EPV + i] = acc[i];
+  for (int j = 0; j < QG; ++j) {
+    if (gl == 0) { sm_m[j][gid] = m[j]; sm_l[j][gid] = l[j]; }
+#pragma unroll
+    for (int i = 0; i < E2; ++i) {
+      sm_acc[((size_t)j * NG + gid) * D + gl * EPV + 2 * i] = acc[j][i].x;
+      sm_acc[((size_t)j * NG + gid) * D + gl * EPV + 2 * i + 1] = acc[j][i].y;
+    }
+  }
   __syncthreads();
-  float M = -INFINITY;
-  for (int g = 0; g < NG; ++g) M = fmaxf(M, sm_m[g]);
-  float L = 0.f;
-  for (int g = 0; g < NG; ++g)
-    if (sm_m[g] != -INFINITY) L += sm_l[g] * __expf(sm_m[g] - M);
-  if (nsplit == 1) {
-    const bool valid = L > 0.f;
-    const float inv = valid ? 1.f / L : 0.f;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-      float a = 0.f;
-      if (valid)
-        for (int g = 0; g < NG; ++g)
-          if (sm_m[g] != -INFINITY) a += sm_acc[g * D + d] * __expf(sm_m[g] - M);
-      o[bh * D + d] = Elem<T>::from(a * inv);
-    }
-    if (threadIdx.x == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
-  } else {
-    float* rec = ws + (bh * nsplit + split) * (size_t)(D + 2);
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-      float a = 0.f;
-      for (int g = 0; g < NG; ++g)
-        if (sm_m[g] != -INFINITY) a += sm_acc[g * D + d] * __expf(sm_m[g] - M);
+  for (int idx = threadIdx.x; idx < QG * D; idx += blockDim.x) {
+    const int j = idx / D, d = idx % D;
+    float M = -INFINITY;
+    for (int g = 0; g < NG; ++g) M = fmaxf(M, sm_m[j][g]);
+    float L = 0.f, a = 0.f;
+    for (int g = 0; g < NG; ++g)
+      if (sm_m[j][g] != -INFINITY) {
+        const float w = __expf(sm_m[j][g] - M);
+        L += sm_l[j][g] * w;
+        a += sm_acc[((size_t)j * NG + g) * D + d] * w;
+      }
+    const size_t bh = bh0 + j;
+    if (nsplit == 1) {
+      const bool valid = L > 0.f;
+      o[bh * D + d] = Elem<T>::from(valid ? a / L : 0.f);
+      if (d == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
+    } else {
+      float* rec = ws + (bh * nsplit + split) * (size_t)(D + 2);
       rec[2 + d] = a;
+      if (d == 0) { rec[0] = M; rec[1] = L; }
     }
-    if (threadIdx.x == 0) { rec[0] = M; rec[1] = L; }
   }
 }
 
@@ -235,23 +274,24 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws, T* __restrict_
   if (threadIdx.x == 0 && lse) lse[bh] = valid ? M + logf(L) : 0.f;
 }
 
-template <typename T, int G, typename Keys>
+template <typename T, int G, int QG, typename Keys>
 int launch_decode(const void* q, const void* k, const void* v, void* o, float* lse, float* ws,
                   int BH, int D, float scale, const Keys& keys, int64_t kv_rows, int nsplit,
-                  cudaStream_t s) {
+                  int heads, int group, cudaStream_t s) {
   constexpr int NG = (kDecThreads / 32) * (32 / G);
-  const size_t sm = sizeof(float) * NG * D;
-  auto kern = decode_split_kernel<T, G, Keys>;
+  constexpr int U = 4;   // keys in flight per lane group
+  const size_t sm = sizeof(float) * QG * NG * D;
+  auto kern = decode_split_kernel<T, G, QG, U, Keys>;
   if (sm > 48 * 1024) {
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)sm), "cudaFuncSetAttribute(decode)"))
       return rc;
   }
-  dim3 grid(nsplit, BH);
+  dim3 grid(nsplit, BH / QG);
   {
     LaunchScope ls("decode_split_kernel", s);
     kern<<<grid, kDecThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, ws,
-                                       D, scale, keys, kv_rows, nsplit);
+                                       D, scale, keys, kv_rows, nsplit, heads, group);
   }
   if (int rc = check_launch("decode_split_kernel")) return rc;
   if (nsplit > 1) {
@@ -264,37 +304,55 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, float* l
   return SBFA_OK;
 }
 
-template <typename T, typename Keys>
-int dispatch_decode(int G, const void* q, const void* k, const void* v, void* o, float* lse,
-                    float* ws, int BH, int D, float scale, const Keys& keys, int64_t kv_rows,
-                    int nsplit, cudaStream_t s) {
-  switch (G) {
-    case 1: return launch_decode<T, 1>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
-    case 2: return launch_decode<T, 2>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
-    case 4: return launch_decode<T, 4>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
-    case 8: return launch_decode<T, 8>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
-    case 16:
-      return launch_decode<T, 16>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
-    case 32:
-      return launch_decode<T, 32>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, s);
+template <typename T, int G, typename Keys>
+int launch_decode_qg(int qg, const void* q, const void* k, const void* v, void* o, float* lse,
+                     float* ws, int BH, int D, float scale, const Keys& keys, int64_t kv_rows,
+                     int nsplit, int heads, int group, cudaStream_t s) {
+  switch (qg) {
+    case 1: return launch_decode<T, G, 1>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, heads, group, s);
+    case 2: return launch_decode<T, G, 2>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, heads, group, s);
+    case 4: return launch_decode<T, G, 4>(q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows, nsplit, heads, group, s);
   }
+  return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported heads per CTA");
+}
+
+template <typename T, typename Keys>
+int dispatch_decode(int G, int qg, const void* q, const void* k, const void* v, void* o,
+                    float* lse, float* ws, int BH, int D, float scale, const Keys& keys,
+                    int64_t kv_rows, int nsplit, int heads, int group, cudaStream_t s) {
+#define SBFA_DEC(GG)                                                                          \
+  case GG:                                                                                    \
+    return launch_decode_qg<T, GG>(qg, q, k, v, o, lse, ws, BH, D, scale, keys, kv_rows,       \
+                                   nsplit, heads, group, s);
+  switch (G) {
+    SBFA_DEC(1)
+    SBFA_DEC(2)
+    SBFA_DEC(4)
+    SBFA_DEC(8)
+    SBFA_DEC(16)
+    SBFA_DEC(32)
+  }
+#undef SBFA_DEC
   return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported head_dim for the vector layout");
 }
 
 template <typename Keys>
 int decode_any(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const Keys& keys, int64_t kv_rows,
-               int nsplit, cudaStream_t s) {
+               int nsplit, int heads, int group, cudaStream_t s) {
   const int G = decode_group(dtype, D);
+  const int qg = decode_heads_per_cta(group);
   float* w = (float*)ws;
   switch (dtype) {
     case SBFA_F16:
-      return dispatch_decode<__half>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows, nsplit, s);
+      return dispatch_decode<__half>(G, qg, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows,
+                                     nsplit, heads, group, s);
     case SBFA_BF16:
-      return dispatch_decode<__nv_bfloat16>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows,
-                                            nsplit, s);
+      return dispatch_decode<__nv_bfloat16>(G, qg, q, k, v, o, lse, w, BH, D, scale, keys,
+                                            kv_rows, nsplit, heads, group, s);
     case SBFA_F32:
-      return dispatch_decode<float>(G, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows, nsplit, s);
+      return dispatch_decode<float>(G, qg, q, k, v, o, lse, w, BH, D, scale, keys, kv_rows,
+                                    nsplit, heads, group, s);
   }
   return fail(SBFA_ERR_UNSUPPORTED, "decode: unsupported dtype");
 }
@@ -326,11 +384,25 @@ int decode_group(int dtype, int64_t D) {
   return 0;
 }
 
-// Number of splits per (b, h): enough CTAs for ~16 per SM, never more than
-// the tiles a row can hold.
-int decode_nsplit(int64_t BH, int64_t est_tiles) {
-  int64_t target = 148 * 16;
-  int64_t ns = (target + BH - 1) / BH;
+int device_sm_count();
+
+// Query heads one CTA serves for a grouped-query factor: the largest power
+// of two up to 4 that divides the group (1 without grouping).  Four keeps
+// the kernel at ~150 registers, three CTAs (12 warps, 48 KB of loads in
+// flight) per SM; eight would need ~250 and leave two.  A group of 8 is
+// served by two CTAs side by side, whose second read of each row is mostly
+// an L2 hit.
+int decode_heads_per_cta(int group) {
+  for (int qg = 4; qg > 1; qg >>= 1)
+    if (group % qg == 0) return qg;
+  return 1;
+}
+
+// Number of splits per (b, h): enough CTAs for ~16 per SM of this device
+// over `ctas` CTAs per split, never more than the tiles a row can hold.
+int decode_nsplit(int64_t ctas, int64_t est_tiles) {
+  const int64_t target = (int64_t)device_sm_count() * 16;
+  int64_t ns = (target + ctas - 1) / std::max<int64_t>(1, ctas);
   ns = std::max<int64_t>(1, std::min<int64_t>(ns, std::max<int64_t>(1, est_tiles)));
   return (int)std::min<int64_t>(ns, 64);
 }
@@ -341,9 +413,10 @@ int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit) {
 
 int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
-               const int32_t* ci, int nsplit, cudaStream_t s) {
+               const int32_t* ci, int nsplit, int heads, int group, cudaStream_t s) {
   const PlanKeys keys{mp, rp, ci};
-  return decode_any(dtype, q, k, v, o, lse, ws, BH, D, scale, keys, (int64_t)mp.n_kv, nsplit, s);
+  return decode_any(dtype, q, k, v, o, lse, ws, BH, D, scale, keys, (int64_t)mp.n_kv, nsplit,
+                    heads, group, s);
 }
 
 }  // namespace sbfa
@@ -389,10 +462,11 @@ extern "C" int sbfa_decode_noalloc(const void* q, const void* k, const void* v, 
                                    const int32_t* block_mask, int64_t block_m, int64_t block_n,
                                    void* stream) {
   using namespace sbfa;
-  if (B <= 0 || H <= 0 || n_kv <= 0 || head_dim <= 0)
-    return fail(SBFA_ERR_INVALID, "B, H, n_kv and head_dim must be positive");
-  if (sink < 0 || window < 0)
-    return fail(SBFA_ERR_INVALID, "sink_size and window_size must be non-negative");
+  // the same checks as sbfa_decode, all before anything touches the shared
+  // scratch or launches a kernel
+  if (int rc = check_decode_args(q, k, v, o, B, H, n_kv, head_dim, dtype, sink, window,
+                                 block_mask, block_m, block_n, H))
+    return rc;
   const int64_t n_tiles = (n_kv + kDecTile - 1) / kDecTile;
   // plan: row_ptr[2], col_idx[n_tiles], nnz[1]; partials start on a 256-byte boundary
   const int64_t plan_bytes = ((2 + n_tiles + 1) * (int64_t)sizeof(int32_t) + 255) / 256 * 256;
@@ -417,7 +491,7 @@ extern "C" int sbfa_decode_noalloc(const void* q, const void* k, const void* v, 
     return rc;
   return sbfa_decode(q, k, v, o, lse, B, H, n_kv, head_dim, dtype, softmax_scale, is_causal, sink,
                      window, block_mask, block_m, block_n, row_ptr, col_idx,
-                     ws_bytes > 0 ? base + plan_bytes : nullptr, ws_bytes, stream);
+                     ws_bytes > 0 ? base + plan_bytes : nullptr, ws_bytes, H, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -549,5 +623,6 @@ extern "C" int sbfa_ring_decode(const void* q, const void* k_cache, const void* 
     return fail(SBFA_ERR_INVALID, "sbfa_ring_decode: split workspace too small (need " +
                                       std::to_string(need) + " bytes)");
   return decode_any(dtype, q, k_cache, v_cache, o, lse, split_ws, (int)BH, (int)head_dim,
-                    (float)softmax_scale, keys, sink + window, ns, (cudaStream_t)stream);
+                    (float)softmax_scale, keys, sink + window, ns, (int)H, 1,
+                    (cudaStream_t)stream);
 }

@@ -48,7 +48,7 @@ _SIGNATURES = {
                   _i64, _i32, _f64, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
                   _vp, _i64, _vp], _i32),
     "sbfa_decode": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f64, _i32, _i64,
-                     _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _i32),
+                     _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp], _i32),
     "sbfa_decode_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "sbfa_selftest_wait_timeout": ([_i64, _vp], _i32),
     "sbfa_ring_append": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i64,

@@ -282,7 +282,7 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
         code = native.dtype_code(q.dtype)
         L = native.lib()
         kv_heads = int(k.shape[1])
-        decode = N_Q == 1 and kv_heads == H and bool(L.sbfa_decode_supported(code, D))
+        decode = N_Q == 1 and bool(L.sbfa_decode_supported(code, D))
         if decode:  # the decode kernel reads contiguous q / k / v
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         else:       # strided views are read in place
@@ -301,7 +301,7 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                     B, H, N_KV, D, code, float(softmax_scale), int(bool(is_causal)),
                     int(sink_size), int(window_size), block_mask.data_ptr(), block_m, block_n,
                     plan["row_ptr"].data_ptr(), plan["col_idx"].data_ptr(), ws.data_ptr(),
-                    ws.numel(), stream), "decode")
+                    ws.numel(), kv_heads, stream), "decode")
             else:
                 plan = _plan_for(block_mask, 0, q.dtype, D, N_Q, N_KV, block_m, block_n)
                 native.check(L.sbfa_fwd(
@@ -360,7 +360,8 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     kept block also applies the StreamingLLM token rule with
     ``sink_size`` / ``window_size``.  ``softmax_scale`` defaults to
     ``1/sqrt(D)``.  A single query (``N_Q == 1``) runs the split-KV decode
-    kernel.
+    kernel, which with grouped K/V heads reads each K/V row once for all the
+    query heads of its group.
     """
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(q.shape[-1])

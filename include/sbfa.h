@@ -4,9 +4,15 @@
  *
  * Conventions shared by every entry point
  *   - All tensor pointers are DEVICE pointers on the current CUDA device.
- *   - Q/K/V/O/dO/dQ/dK/dV are contiguous [B, H, N, D] row-major; LSE and
- *     Delta are contiguous fp32 [B, H, N_Q].  (The upstream Python bridge
- *     forces .contiguous() on its inputs, sparse_triton_kernel.py:834,707.)
+ *   - Q/K/V/O/dO/dQ/dK/dV are logical [B, H, N, D] tensors with a unit-stride
+ *     last dimension.  sbfa_fwd and sbfa_bwd take an optional host array of
+ *     (batch, head, row) element strides per tensor (NULL = contiguous), so
+ *     transposed views are read and written in place; the tensor-core kernels
+ *     (float16/bfloat16, head_dim 64 or 128) then need 16-byte aligned
+ *     tensors whose strides are positive multiples of 8 elements.  The decode
+ *     and ring-cache entry points take contiguous tensors.  LSE and Delta are
+ *     always contiguous fp32 [B, H, N_Q].  (The upstream Python bridge forces
+ *     .contiguous() on every input, sparse_triton_kernel.py:834,707.)
  *   - `stream` is a cudaStream_t passed as void*; every launch is
  *     asynchronous on it.  NULL means the legacy default stream.
  *   - Return value: SBFA_OK (0) or an SBFA_ERR_* code; sbfa_last_error()
@@ -179,15 +185,17 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
  * N_Q = 1, BLOCK_M = 1: benchmark.py:799-804 -> sparse_triton_kernel.py:231).
  * Reads only the K/V rows the query can see.  row_ptr/col_idx: plan of
  * pass 3.  split_ws: caller scratch of sbfa_decode_workspace_bytes() bytes.
- * lse may be NULL. */
+ * lse may be NULL.  q, o: contiguous [B, H, 1, D]; k, v: contiguous
+ * [B, kv_heads, n_kv, D] (kv_heads <= 0 means H); with kv_heads < H each
+ * K/V row is read once for all the query heads of its group. */
 int sbfa_decode(const void* q, const void* k, const void* v, void* o, float* lse,
                 int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
                 double softmax_scale, int is_causal, int64_t sink, int64_t window,
                 const int32_t* block_mask, int64_t block_m, int64_t block_n,
                 const int32_t* row_ptr, const int32_t* col_idx, void* split_ws,
-                int64_t split_ws_bytes, void* stream);
+                int64_t split_ws_bytes, int64_t kv_heads, void* stream);
 
-/* Scratch bytes sbfa_decode needs for this shape. */
+/* Scratch bytes sbfa_decode needs for this shape (any kv_heads). */
 int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
                                     int64_t head_dim, int64_t block_n);
 

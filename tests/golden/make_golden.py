@@ -16,7 +16,10 @@ own tests use plus the five benchmark configurations:
   popcount, per-row counts and a SHA-256 of the packed bits;
 * ``attention_cases.npz`` - ``reference_block_sparse_attention``
   (ref ``:845-902``) outputs and autograd dQ/dK/dV in float64 on seeded
-  inputs (the inputs are stored too, so no RNG agreement is assumed).
+  inputs (the inputs are stored too, so no RNG agreement is assumed);
+* ``attention_tc_cases.npz`` - the same for inputs rounded to bfloat16 /
+  float16 at head_dim 128 / 64 with 128 x 128 blocks, the shapes the
+  tensor-core kernels take (``--tc-only`` regenerates just this file).
 
 The fixtures are committed; the GPU box never needs the upstream tree.
 """
@@ -81,6 +84,21 @@ ATTN_CASES = [
     ("window_only", 1, 2, 64, 64, 16, 16, 16, True, 0, 64, "streaming"),
     ("custom_empty_row", 1, 2, 32, 32, 16, 16, 16, False, 0, 0, "custom_empty_row"),
     ("custom_causal", 1, 1, 96, 160, 16, 32, 32, True, 4, 48, "custom_random"),
+]
+
+
+# Cases that reach the tensor-core kernels (float16 / bfloat16, head_dim 64 or
+# 128, BM = BN = 128): (name, B, H, n_q, n_kv, D, bm, bn, is_causal, S, W,
+# mask_kind, dtype).  Inputs are drawn in float64, rounded to the 16-bit type
+# and stored as that type's bit patterns; the upstream reference runs in
+# float64 on the rounded values and its outputs are stored as float32.
+ATTN_TC_CASES = [
+    ("tc_bf16_streaming_d128", 1, 1, 384, 384, 128, 128, 128, True, 4, 160, "streaming",
+     "bfloat16"),
+    ("tc_fp16_bottom_right_d64", 1, 1, 200, 456, 64, 128, 128, True, 4, 200, "streaming",
+     "float16"),
+    ("tc_fp16_custom_noncausal_d128", 1, 1, 256, 256, 128, 128, 128, False, 0, 0,
+     "custom_antidiagonal", "float16"),
 ]
 
 
@@ -160,10 +178,49 @@ def main(root: str) -> None:
                       ("dq", qq.grad), ("dk", kk.grad), ("dv", vv.grad)):
             att[p + nm] = t.numpy()
     np.savez_compressed(os.path.join(HERE, "attention_cases.npz"), **att)
+    main_tc(up)
     print("wrote", sorted(os.listdir(HERE)))
 
 
+def main_tc(up) -> None:
+    """attention_tc_cases.npz: ATTN_TC_CASES through the upstream reference."""
+    att = {}
+    for (name, B, H, n_q, n_kv, D, bm, bn, causal, s, w, kind, dt) in ATTN_TC_CASES:
+        tdt = getattr(torch, dt)
+        g = torch.Generator().manual_seed(4321)
+        ins = [torch.randn(B, H, n, D, generator=g, dtype=torch.float64).to(tdt)
+               for n in (n_q, n_kv, n_kv, n_q)]
+        q, k, v, do = (t.double() for t in ins)
+        n_qb, n_kb = -(-n_q // bm), -(-n_kv // bn)
+        if kind == "streaming":
+            mask = up.make_streaming_mask(n_q, n_kv, up.StreamingMaskSpec(s, w), bm, bn,
+                                          device="cpu")
+        else:  # row block i keeps only key block n_kb - 1 - i: every 256-row
+            # forward tile then holds two partial tiles
+            mask = torch.zeros((n_qb, n_kb), dtype=torch.int32)
+            for i in range(n_qb):
+                mask[i, n_kb - 1 - i] = 1
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = up.reference_block_sparse_attention(
+            qq, kk, vv, mask, block_m=bm, block_n=bn, is_causal=causal,
+            sink_size=s, window_size=w)
+        o.backward(do)
+        p = f"{name}__"
+        att[p + "params"] = np.array([B, H, n_q, n_kv, D, bm, bn, int(causal), s, w],
+                                     dtype=np.int64)
+        att[p + "dtype"] = np.array(dt)
+        att[p + "mask"] = mask.numpy().astype(np.int32)
+        for nm, t in zip(("q", "k", "v", "do"), ins):
+            att[p + nm] = t.view(torch.int16).numpy()
+        for nm, t in (("o", o.detach()), ("dq", qq.grad), ("dk", kk.grad), ("dv", vv.grad)):
+            att[p + nm] = t.float().numpy()
+    np.savez_compressed(os.path.join(HERE, "attention_tc_cases.npz"), **att)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: make_golden.py <upstream checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3) or (len(sys.argv) == 3 and sys.argv[2] != "--tc-only"):
+        raise SystemExit("usage: make_golden.py <upstream checkout> [--tc-only]")
+    if len(sys.argv) == 3:
+        main_tc(load_upstream(sys.argv[1]))
+    else:
+        main(sys.argv[1])

@@ -44,7 +44,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.sbfa_abi_version() == 3
+    assert lib.sbfa_abi_version() == 4
 
 
 def test_validation_errors_without_gpu(lib):

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from oracle import streaming_oracle as orc
-from tests.golden.make_golden import (ATTN_CASES, BLOCK_CASES, DENSE_CASES,
+from tests.golden.make_golden import (ATTN_CASES, ATTN_TC_CASES, BLOCK_CASES, DENSE_CASES,
                                       TOKEN_CASES, key_block)
 
 
@@ -77,6 +77,31 @@ def test_attention_forward_backward_matches_reference(attn, name):
         is_causal=bool(causal), sink_size=s, window_size=w)
     for nm, got in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
         assert torch.allclose(got, t[nm], atol=1e-12, rtol=1e-12), nm
+
+
+def tc_case_inputs(g, name: str):
+    """Inputs of a tensor-core golden case as tensors of their 16-bit type,
+    plus the case parameters and the stored float32 reference outputs."""
+    p = f"{name}__"
+    params = g[p + "params"].tolist()
+    dt = getattr(torch, str(g[p + "dtype"]))
+    ins = {k: torch.from_numpy(g[p + k]).view(dt) for k in ("q", "k", "v", "do")}
+    outs = {k: torch.from_numpy(g[p + k]) for k in ("o", "dq", "dk", "dv")}
+    return params, dt, g[p + "mask"], ins, outs
+
+
+@pytest.mark.parametrize("name", [c[0] for c in ATTN_TC_CASES])
+def test_tensor_core_cases_match_reference(golden_dir, name):
+    """The oracle in float64 on the 16-bit inputs reproduces the upstream
+    outputs stored for the tensor-core shapes (stored as float32)."""
+    g = np.load(os.path.join(golden_dir, "attention_tc_cases.npz"))
+    (B, H, n_q, n_kv, D, bm, bn, causal, s, w), dt, mask, ins, outs = tc_case_inputs(g, name)
+    assert dt in (torch.float16, torch.bfloat16) and D in (64, 128) and bm == bn == 128
+    o, dq, dk, dv = orc.attention_forward_backward(
+        *(ins[k].double() for k in ("q", "k", "v", "do")), mask, block_m=bm, block_n=bn,
+        is_causal=bool(causal), sink_size=s, window_size=w)
+    for nm, got in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        assert torch.allclose(got.float(), outs[nm], atol=1e-6, rtol=1e-6), nm
 
 
 def test_empty_rows_are_zero_in_golden(attn):
