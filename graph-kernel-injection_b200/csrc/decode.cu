@@ -37,6 +37,26 @@ namespace {
 constexpr int kDecThreads = 128;
 constexpr int kDecTile = 64;   // keys per plan tile (pass 3)
 
+// Grouped-query decode tuning: query heads per CTA at most (1, 2 or 4), keys
+// per lane group and iteration, and whether the next iteration's rows are
+// loaded before the current one is computed.  Measured at config-4 geometry
+// with 8 and 4 K/V heads (fp16, B=64): 4 heads, 2 keys, prefetch 2498 GB/s;
+// 4 heads, 4 keys 2392; 4 heads, 4 keys, prefetch 2106; 2 heads, 4 keys
+// 2231; one head per CTA (rows re-read per query head) 1753.
+#ifndef SBFA_DECODE_MAX_QG
+#define SBFA_DECODE_MAX_QG 4
+#endif
+#ifndef SBFA_DECODE_GQA_UNROLL
+#define SBFA_DECODE_GQA_UNROLL 2
+#endif
+#ifndef SBFA_DECODE_GQA_PREFETCH
+#define SBFA_DECODE_GQA_PREFETCH 1
+#endif
+constexpr int kMaxQG = SBFA_DECODE_MAX_QG;
+constexpr int kGqaUnroll = SBFA_DECODE_GQA_UNROLL;
+constexpr bool kGqaPrefetch = SBFA_DECODE_GQA_PREFETCH != 0;
+static_assert(kMaxQG == 1 || kMaxQG == 2 || kMaxQG == 4, "heads per CTA: 1, 2 or 4");
+
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& w, float* f) {
   if constexpr (sizeof(T) == 2) {
@@ -97,7 +117,7 @@ struct RingKeys {
 // used by all QG queries.  Lane l of a G-lane group holds elements
 // [l*EPV, (l+1)*EPV) of the row for every one of the QG queries; dot
 // products and accumulators use packed fp32x2 FMAs.
-template <typename T, int G, int QG, int U, typename Keys>
+template <typename T, int G, int QG, int U, bool PF, typename Keys>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     T* __restrict__ o, float* __restrict__ lse, float* __restrict__ ws, int D, float scale,
@@ -145,10 +165,11 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
     for (int i = 0; i < E2; ++i) acc[j][i] = make_float2(0.f, 0.f);
   }
 
+  // U keys per lane group and iteration; with PF the next iteration's rows
+  // are requested before this one's arithmetic, so loads stay in flight
+  // while the CTA computes.
   const int step = NG * U;
-  for (int base = 0; base < total; base += step) {
-    uint4 kw[U], vw[U];
-    bool vis[U];
+  auto fetch = [&](int base, uint4 (&kw)[U], uint4 (&vw)[U], bool (&vis)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = base + u * NG + gid;
@@ -163,6 +184,24 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(
           vw[u] = __ldg(vb + (size_t)key * vec_per_row + gl);
         }
       }
+    }
+  };
+  uint4 kn[U], vn[U];
+  bool visn[U];
+  if (PF) fetch(0, kn, vn, visn);
+  for (int base = 0; base < total; base += step) {
+    uint4 kw[U], vw[U];
+    bool vis[U];
+    if (PF) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        kw[u] = kn[u];
+        vw[u] = vn[u];
+        vis[u] = visn[u];
+      }
+      if (base + step < total) fetch(base + step, kn, vn, visn);
+    } else {
+      fetch(base, kw, vw, vis);
     }
     float s[U][QG];
 #pragma unroll
@@ -279,9 +318,10 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, float* l
                   int BH, int D, float scale, const Keys& keys, int64_t kv_rows, int nsplit,
                   int heads, int group, cudaStream_t s) {
   constexpr int NG = (kDecThreads / 32) * (32 / G);
-  constexpr int U = 4;   // keys in flight per lane group
+  constexpr int U = QG > 1 ? kGqaUnroll : 4;       // keys per lane group and iteration
+  constexpr bool PF = QG > 1 ? kGqaPrefetch : false;
   const size_t sm = sizeof(float) * QG * NG * D;
-  auto kern = decode_split_kernel<T, G, QG, U, Keys>;
+  auto kern = decode_split_kernel<T, G, QG, U, PF, Keys>;
   if (sm > 48 * 1024) {
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)sm), "cudaFuncSetAttribute(decode)"))
@@ -393,7 +433,7 @@ int device_sm_count();
 // served by two CTAs side by side, whose second read of each row is mostly
 // an L2 hit.
 int decode_heads_per_cta(int group) {
-  for (int qg = 4; qg > 1; qg >>= 1)
+  for (int qg = kMaxQG; qg > 1; qg >>= 1)
     if (group % qg == 0) return qg;
   return 1;
 }
