@@ -313,24 +313,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // (rare after the first tiles) is redone below.  A row with nothing
       // visible so far has only -inf scores, so m_use = 0 gives p = 0.
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float mx[8], acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float mx[4];
+      float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t pk[kHalf / 2];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
+      const float2 sc2 = make_float2(scale_log2, scale_log2);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+      // packed fp32x2 arithmetic (masked scores are -inf: 2^-inf = 0)
 #pragma unroll
       for (int i = 0; i < kHalf / 2; ++i) {
         const float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
-        mx[i & 7] = fmaxf(mx[i & 7], fmaxf(s0, s1));
-        const float p0 = ex2(fmaf(s0, scale_log2, -m_use));
-        const float p1 = ex2(fmaf(s1, scale_log2, -m_use));
-        acc[i & 3] += p0 + p1;
-        pk[i] = pack2<T>(p0, p1);
+        mx[i & 3] = max3f(mx[i & 3], s0, s1);
+        const float2 x2 = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
+        const float2 p = make_float2(ex2(x2.x), ex2(x2.y));
+        acc[i & 1] = __fadd2_rn(acc[i & 1], p);
+        pk[i] = pack2<T>(p.x, p.y);
       }
-      const float rm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float rm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float m_new = rm * scale_log2;
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
-      float rsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      float rsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       if (!__any_sync(0xffffffffu, need)) {
         tmem_st16(t_s, pk);
         tmem_st16(t_s + 16u, pk + 16);

@@ -718,12 +718,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // dS = P * (dP - Delta); the softmax scale multiplies dQ in the epilogue
       uint32_t ds2[32];
       if (all_vis) {
+        // packed fp32x2 arithmetic for the exponents and dS
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const float2 nl2 = make_float2(-lse2, -lse2), nd2 = make_float2(-dl, -dl);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2(fmaf(__uint_as_float(sv[2 * c]), scale_log2, -lse2));
-          const float p1 = ex2(fmaf(__uint_as_float(sv[2 * c + 1]), scale_log2, -lse2));
-          ds2[c] = pack2<T>(p0 * (__uint_as_float(dpv[2 * c]) - dl),
-                            p1 * (__uint_as_float(dpv[2 * c + 1]) - dl));
+          const float2 x = __ffma2_rn(
+              make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nl2);
+          const float2 p = make_float2(ex2(x.x), ex2(x.y));
+          const float2 d = __fmul2_rn(
+              p, __fadd2_rn(make_float2(__uint_as_float(dpv[2 * c]),
+                                        __uint_as_float(dpv[2 * c + 1])),
+                            nd2));
+          ds2[c] = pack2<T>(d.x, d.y);
         }
       } else {
 #pragma unroll

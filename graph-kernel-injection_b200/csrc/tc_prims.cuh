@@ -306,6 +306,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Largest of three floats in one instruction.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
