@@ -109,7 +109,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                    T* __restrict__ dv, const float* __restrict__ lse,
                    const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
                    const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
-                   int n_tj, int heads, int kv_group, Strides3 sdk, Strides3 sdv, int* status) {
+                   int n_tj, int heads, int kv_group, Strides3 sdk, Strides3 sdv,
+                   float* __restrict__ part_ws, int sink_parts, int* status) {
   using L = DkdvLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
@@ -133,16 +134,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // BH counts (batch, key/value head) units.  The sink key tiles (seen by
-  // every query tile) first, one per unit; then each unit's remaining key
-  // tiles in order, so CTAs running side by side stream the same query tiles
-  // through L2.  With grouped-query attention the kv_group query heads of a
-  // unit are streamed one after another and all accumulate into its dK, dV.
-  int tj, bh;
-  if ((int)blockIdx.x < BH) {
+  // every query tile) first; then each unit's remaining key tiles in order,
+  // so CTAs running side by side stream the same query tiles through L2.
+  // With grouped-query attention the kv_group query heads of a unit are
+  // streamed one after another and all accumulate into its dK, dV, except
+  // for the sink tile when sink_parts > 1: its column is as long as the
+  // whole sequence for every query head of the group, so sink_parts CTAs per
+  // unit take one query head each and leave fp32 partial dV, dK in part_ws
+  // for dkdv_sink_reduce_kernel.
+  int tj, bh, head_lo = 0, n_heads = kv_group;
+  bool split = false;
+  if ((int)blockIdx.x < BH * sink_parts) {
     tj = 0;
-    bh = blockIdx.x;
+    bh = blockIdx.x / sink_parts;
+    if (sink_parts > 1) {
+      split = true;
+      head_lo = blockIdx.x % sink_parts;
+      n_heads = 1;
+    }
   } else {
-    const int idx = blockIdx.x - BH;
+    const int idx = blockIdx.x - BH * sink_parts;
     bh = idx / (n_tj - 1);
     tj = 1 + idx % (n_tj - 1);
   }
@@ -150,8 +161,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int hh = bh % kv_heads, bb = bh / kv_heads;  // TMA coordinates of the K/V plane
   const int e0 = col_ptr[tj];
   const int nq = col_ptr[tj + 1] - e0;   // query tiles per query head
-  const int ntot = nq * kv_group;        // streamed tiles: (head j, tile) = (i / nq, i % nq)
+  // streamed tiles: tile i is query tile i % nq of query head
+  // hh * kv_group + head_lo + i / nq
+  const int ntot = nq * n_heads;
+  // partials of this CTA when split: [dV | dK] x 128 keys x D fp32
+  float* part = split ? part_ws + (size_t)blockIdx.x * 2 * kT * D : nullptr;
 
+  if (nq == 0 && split) {  // no query sees the sink tile: zero partials
+    for (int idx = threadIdx.x; idx < 2 * kT * D / 4; idx += blockDim.x)
+      reinterpret_cast<float4*>(part)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
   if (nq == 0) {  // no query sees this key tile: dK = dV = 0
     for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
       const int rr = idx / (D / 8), cc = idx % (D / 8);
@@ -210,7 +230,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = true;
       for (int i = 0; ok && i < ntot; ++i) {
         const int ti = plan_index(next_ent);
-        const int hq = hh * kv_group + i / nq;  // query head of tile i
+        const int hq = hh * kv_group + head_lo + i / nq;  // query head of tile i
         if (i + 1 < ntot) next_ent = row_idx[e0 + (i + 1) % nq];  // prefetch the next entry
         for (int part = 0; part < 2; ++part) {           // Q_i, then dO_i
           const int e = 2 * i + part, s = e % L::kRing, f = e / L::kRing;
@@ -243,7 +263,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int slot = i & 1;
         const int ti = plan_index(row_idx[e0 + i % nq]);
         const int row0 = ti * kT;
-        const size_t qbh = (size_t)bb * heads + hh * kv_group + i / nq;  // query (b, h)
+        const size_t qbh = (size_t)bb * heads + hh * kv_group + head_lo + i / nq;  // query (b, h)
         float lv[kT / 32], dv2[kT / 32];
 #pragma unroll
         for (int c = 0; c < kT / 32; ++c) {  // loads first, then the wait for the slot
@@ -430,6 +450,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // dK * scale (staged in V's buffer); both buffers are free once every
     // MMA is done
     if (ok) ok = wait_bar_w(bar(L::kDone), 0, abort_flag, status);
+    if (ok && split) {
+      // one part of a split sink tile: raw fp32 dV (group 0) / dK (group 1)
+      // rows straight from TMEM, summed and scaled by dkdv_sink_reduce_kernel
+      tc_fence_after();
+      const uint32_t t_acc = tmem + lane_base + (grp == 0 ? kTDV : kTDK);
+      float4* dst = reinterpret_cast<float4*>(part + ((size_t)grp * kT + r) * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(t_acc + 32u * c, t);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i2 = 0; i2 < 8; ++i2)
+          dst[8 * c + i2] = make_float4(__uint_as_float(t[4 * i2]), __uint_as_float(t[4 * i2 + 1]),
+                                        __uint_as_float(t[4 * i2 + 2]),
+                                        __uint_as_float(t[4 * i2 + 3]));
+      }
+      ok = false;  // nothing left to store
+    }
     if (ok) {
       tc_fence_after();
       const uint32_t t_acc = tmem + lane_base + (grp == 0 ? kTDV : kTDK);
@@ -471,6 +510,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// dV, dK of the sink key tile of every (batch, key/value head) unit from the
+// fp32 partials of its `parts` CTAs (one per query head of the group):
+// summed in part order, dK scaled, rounded to 16 bits, rows past n_kv
+// skipped.  One CTA per unit.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) dkdv_sink_reduce_kernel(
+    const float* __restrict__ part_ws, T* __restrict__ dk, T* __restrict__ dv, int parts,
+    int kv_heads, int n_kv, float scale, Strides3 sdk, Strides3 sdv) {
+  const int u = blockIdx.x;
+  const int hh = u % kv_heads, bb = u / kv_heads;
+  const float4* base = reinterpret_cast<const float4*>(part_ws) + (size_t)u * parts * 2 * kT * D / 4;
+  for (int idx = threadIdx.x; idx < kT * D / 4; idx += blockDim.x) {
+    const int key = idx / (D / 4), c4 = idx % (D / 4);
+    if (key >= n_kv) continue;
+    float4 sv = make_float4(0.f, 0.f, 0.f, 0.f), sk = sv;
+    for (int p = 0; p < parts; ++p) {
+      const float4 a = base[(size_t)p * 2 * kT * D / 4 + idx];
+      const float4 b = base[(size_t)p * 2 * kT * D / 4 + kT * D / 4 + idx];
+      sv = make_float4(sv.x + a.x, sv.y + a.y, sv.z + a.z, sv.w + a.w);
+      sk = make_float4(sk.x + b.x, sk.y + b.y, sk.z + b.z, sk.w + b.w);
+    }
+    const uint2 ov = make_uint2(pack2<T>(sv.x, sv.y), pack2<T>(sv.z, sv.w));
+    const uint2 ok = make_uint2(pack2<T>(sk.x * scale, sk.y * scale),
+                                pack2<T>(sk.z * scale, sk.w * scale));
+    *reinterpret_cast<uint2*>(dv + bb * sdv.b + hh * sdv.h + (int64_t)key * sdv.n + 4 * c4) = ov;
+    *reinterpret_cast<uint2*>(dk + bb * sdk.b + hh * sdk.h + (int64_t)key * sdk.n + 4 * c4) = ok;
   }
 }
 
@@ -796,8 +864,8 @@ template <typename T, int D>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
                   const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
-                  const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
-                  cudaStream_t s) {
+                  const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri,
+                  float* part_ws, int sink_parts, int* status, cudaStream_t s) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv;
@@ -820,13 +888,21 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
       return rc;
     const int n_tj = ceil_div_i(mp.n_kv, kT);
     const int units = BH / vw.kv_group;  // (batch, key/value head) pairs
-    LaunchScope ls("dkdv_tc_kernel", s);
-    kern<<<n_tj * units, kBwdThreads, L::kAlloc, s>>>(mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv,
-                                                     lse, delta, scale, sl, mp, kv_cp, kv_ri,
-                                                     units, n_tj, vw.heads, vw.kv_group, vw.dk,
-                                                     vw.dv, status);
+    {
+      LaunchScope ls("dkdv_tc_kernel", s);
+      kern<<<(n_tj - 1 + sink_parts) * units, kBwdThreads, L::kAlloc, s>>>(
+          mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse, delta, scale, sl, mp, kv_cp, kv_ri,
+          units, n_tj, vw.heads, vw.kv_group, vw.dk, vw.dv, part_ws, sink_parts, status);
+    }
+    if (int rc = check_launch("dkdv_tc_kernel")) return rc;
+    if (sink_parts > 1) {
+      LaunchScope ls("dkdv_sink_reduce_kernel", s);
+      dkdv_sink_reduce_kernel<T, D><<<units, 256, 0, s>>>(part_ws, (T*)dk, (T*)dv, sink_parts,
+                                                          vw.heads / vw.kv_group, mp.n_kv, scale,
+                                                          vw.dk, vw.dv);
+    }
   }
-  if (int rc = check_launch("dkdv_tc_kernel")) return rc;
+  if (int rc = check_launch("dkdv_sink_reduce_kernel")) return rc;
   {
     using L = DqLayout<D>;
     auto kern = dq_tc_kernel<T, D>;
@@ -848,23 +924,40 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
 int generic_delta(int dtype, const void* o, const void* dout, float* delta, int BH, int n_q,
                   int D, const Views& vw, cudaStream_t s);
 
+// Bytes of fp32 partials the split sink tile needs under grouped-query
+// attention (0 without grouping: the sink CTA of a unit then streams a single
+// query head, as every other key tile's CTA does).
+int64_t tc_bwd_split_bytes(int64_t BH, int kv_group, int64_t D) {
+  if (kv_group <= 1) return 0;
+  return BH / kv_group * (int64_t)kv_group * 2 * kT * D * (int64_t)sizeof(float);
+}
+
 int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta, int BH,
            float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
-           const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
-           cudaStream_t s) {
+           const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, void* split_ws,
+           int64_t split_ws_bytes, int* status, cudaStream_t s) {
   if (int rc = generic_delta(dtype, o, dout, delta, BH, mp.n_q, D, vw, s)) return rc;
   const bool bf = dtype == SBFA_BF16;
-  if (D == 128)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
-                                                  mp, vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s)
-              : launch_bwd_tc<__half, 128>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp,
-                                           vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s);
-  if (D == 64)
-    return bf ? launch_bwd_tc<__nv_bfloat16, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale,
-                                                 mp, vw, dq_rp, dq_ci, kv_cp, kv_ri, status, s)
-              : launch_bwd_tc<__half, 64>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw,
-                                          dq_rp, dq_ci, kv_cp, kv_ri, status, s);
+  // split the sink tile over the group's query heads when the caller gave
+  // room for the partials (else one CTA per unit streams every head)
+  const int64_t need = tc_bwd_split_bytes(BH, vw.kv_group, D);
+  const bool split = need > 0 && split_ws != nullptr && split_ws_bytes >= need &&
+                     ((uintptr_t)split_ws & 15u) == 0;
+  float* part = split ? static_cast<float*>(split_ws) : nullptr;
+  const int parts = split ? vw.kv_group : 1;
+#define SBFA_BWD(TT, DD)                                                                        \
+  return launch_bwd_tc<TT, DD>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw, dq_rp, \
+                               dq_ci, kv_cp, kv_ri, part, parts, status, s)
+  if (D == 128) {
+    if (bf) SBFA_BWD(__nv_bfloat16, 128);
+    SBFA_BWD(__half, 128);
+  }
+  if (D == 64) {
+    if (bf) SBFA_BWD(__nv_bfloat16, 64);
+    SBFA_BWD(__half, 64);
+  }
+#undef SBFA_BWD
   return fail(SBFA_ERR_UNSUPPORTED, "tensor-core backward: head_dim must be 64 or 128");
 }
 

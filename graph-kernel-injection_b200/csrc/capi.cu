@@ -43,8 +43,9 @@ int tc_fwd(int dtype, int D, const void* q, const void* k, const void* v, void* 
 int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
            int BH, float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
-           const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, int* status,
-           cudaStream_t s);
+           const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, void* split_ws,
+           int64_t split_ws_bytes, int* status, cudaStream_t s);
+int64_t tc_bwd_split_bytes(int64_t BH, int kv_group, int64_t D);
 namespace tc {
 bool tma_compatible(const void* base, const Strides3& st);
 }
@@ -351,7 +352,7 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
                         int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
                         const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
                         const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
-                        void* stream) {
+                        void* split_ws, int64_t split_ws_bytes, void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
@@ -370,7 +371,7 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
     if (int rc = check_tma(ptrs, st, 7, "sbfa_bwd")) return rc;
     return tc_bwd(dtype, (int)head_dim, q, k, v, o, lse, dout, dq, dk, dv, delta_ws, BH,
                   softmax_scale, mp, vw, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx,
-                  device_status_ptr(), s);
+                  split_ws, split_ws_bytes, device_status_ptr(), s);
   }
   if (!generic_supports(dtype, head_dim))
     return fail(SBFA_ERR_UNSUPPORTED, "head_dim too large (max 256; 128 for float64)");
@@ -403,6 +404,14 @@ int check_decode_args(const void* q, const void* k, const void* v, const void* o
   return SBFA_OK;
 }
 }  // namespace sbfa
+
+extern "C" int64_t sbfa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t head_dim, int dtype,
+                                            int64_t kv_heads) {
+  if (B <= 0 || H <= 0 || head_dim <= 0) return 0;
+  if (kv_heads <= 0) kv_heads = H;
+  if (kv_heads > H || H % kv_heads != 0 || !use_tc(1, dtype, head_dim)) return 0;
+  return tc_bwd_split_bytes(B * H, (int)(H / kv_heads), head_dim);
+}
 
 extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,
                                                int64_t head_dim, int64_t block_n) {

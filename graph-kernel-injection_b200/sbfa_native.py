@@ -46,7 +46,8 @@ _SIGNATURES = {
                   _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _i32),
     "sbfa_bwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                   _i64, _i32, _f64, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
-                  _vp, _i64, _vp], _i32),
+                  _vp, _i64, _vp, _i64, _vp], _i32),
+    "sbfa_bwd_workspace_bytes": ([_i64, _i64, _i64, _i32, _i64], _i64),
     "sbfa_decode": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f64, _i32, _i64,
                      _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp], _i32),
     "sbfa_decode_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),

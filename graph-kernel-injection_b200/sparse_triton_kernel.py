@@ -334,18 +334,23 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
         # the caller's transposes without a copy
         dq, dk, dv = (_readable(torch.empty_like(t), tcore) for t in (q, k, v))
         delta = torch.empty((B, H, N_Q), dtype=torch.float32, device=dev)
+        L = native.lib()
+        kv_heads = int(k.shape[1])
+        code = native.dtype_code(q.dtype)
+        ws_bytes = int(L.sbfa_bwd_workspace_bytes(B, H, D, code, kv_heads))
+        split_ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         with torch.cuda.device(dev):
             p_dq = _plan_for(block_mask, 1, q.dtype, D, N_Q, N_KV, ctx.block_m, ctx.block_n)
             p_kv = _plan_for(block_mask, 2, q.dtype, D, N_Q, N_KV, ctx.block_m, ctx.block_n)
-            native.check(native.lib().sbfa_bwd(
+            native.check(L.sbfa_bwd(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                 do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr(),
-                B, H, N_Q, N_KV, D, native.dtype_code(q.dtype), ctx.softmax_scale,
+                B, H, N_Q, N_KV, D, code, ctx.softmax_scale,
                 int(ctx.is_causal), ctx.sink_size, ctx.window_size, block_mask.data_ptr(),
                 ctx.block_m, ctx.block_n, p_dq["row_ptr"].data_ptr(),
                 p_dq["col_idx"].data_ptr(), p_kv["col_ptr"].data_ptr(),
                 p_kv["row_idx"].data_ptr(), _stride_array(q, k, v, o, do, dq, dk, dv),
-                int(k.shape[1]), native.stream_ptr(dev)), "bwd")
+                kv_heads, native.ptr(split_ws), ws_bytes, native.stream_ptr(dev)), "bwd")
         return dq, dk, dv, None, None, None, None, None, None, None
 
 

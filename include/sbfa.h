@@ -170,7 +170,14 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
  * _bwd_dq_kernel and their launches (sparse_triton_kernel.py:355-601,
  * 694-779).  delta_ws: caller scratch, fp32[B*H*n_q].
  * dq_row_ptr/dq_col_idx: plan of pass 1; kv_col_ptr/kv_row_idx: plan of
- * pass 2 (may be the same plan when the tiles agree). */
+ * pass 2 (may be the same plan when the tiles agree).
+ * split_ws: optional caller scratch (16-byte aligned) of
+ * sbfa_bwd_workspace_bytes() bytes.  With grouped-query attention the first
+ * key tile (the sinks) is seen by every query tile of every query head of a
+ * group; given this scratch, its dK/dV work is split over one CTA per query
+ * head and the fp32 partials are summed by a second kernel, instead of one
+ * CTA streaming all of them.  NULL (or too small) keeps the single CTA;
+ * results agree to rounding. */
 int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              const float* lse, const void* dout, void* dq, void* dk, void* dv,
              float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
@@ -179,7 +186,13 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
              const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
              const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
-             void* stream);
+             void* split_ws, int64_t split_ws_bytes, void* stream);
+
+/* Scratch bytes of the split first key tile in sbfa_bwd (0 when nothing is
+ * split: no grouping, or a dtype / head_dim the tensor-core kernels do not
+ * take).  No upstream counterpart (upstream has no grouped-query attention). */
+int64_t sbfa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t head_dim, int dtype,
+                                 int64_t kv_heads);
 
 /* Split-KV decode for n_q == 1 (the upstream path is _fwd_kernel with
  * N_Q = 1, BLOCK_M = 1: benchmark.py:799-804 -> sparse_triton_kernel.py:231).

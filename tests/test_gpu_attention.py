@@ -264,6 +264,47 @@ def test_grouped_query_decode(dtype, H, Hkv, n_kv, D):
     assert native.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_grouped_query_backward_splits_the_sink_tile(monkeypatch, dtype, D):
+    """With grouped K/V heads the first key tile is seen by every query tile
+    of every query head of its group.  Its dK/dV work is split over one CTA
+    per query head (fp32 partials, summed by a second kernel); the result
+    matches the oracle and the unsplit single-CTA path."""
+    B, H, Hkv, N, S, W = 1, 8, 1, 2048, 4, 256
+    q, k, v, do = (torch.randn(B, h, N, D, generator=torch.Generator(device=DEV).manual_seed(s),
+                               device=DEV, dtype=dtype)
+                   for s, h in ((1, H), (2, Hkv), (3, Hkv), (4, H)))
+    mask = stk.make_streaming_mask(N, N, stk.StreamingMaskSpec(S, W), 128, 128, DEV)
+    L = native.lib()
+    assert L.sbfa_bwd_workspace_bytes(B, H, D, native.dtype_code(dtype), Hkv) > 0
+    native.timing_read()
+    native.timing(True)
+    try:
+        o, dq, dk, dv = run(q, k, v, mask, 128, 128, True, S, W, do=do)
+        ran = native.timing_read()
+    finally:
+        native.timing(False)
+    assert "dkdv_sink_reduce_kernel" in ran, ran
+    # the same call without split scratch: one CTA per unit streams every head
+    monkeypatch.setattr(L, "sbfa_bwd_workspace_bytes", lambda *a: 0)
+    _, dq1, dk1, dv1 = run(q, k, v, mask, 128, 128, True, S, W, do=do)
+    monkeypatch.undo()
+    assert torch.equal(dq, dq1)            # the dQ kernel is untouched
+    for a, b, nm in ((dk, dk1, "dK"), (dv, dv1, "dV")):
+        check_half(a, b.double(), dtype, f"split vs unsplit {nm}")
+    # against the oracle: K/V expanded to every query head, gradients summed
+    # over each group
+    kx, vx = (t.expand(B, H, N, D) for t in (k, v))
+    ro, rdq, rdk, rdv = orc.attention_forward_backward(
+        q.double().cpu(), kx.double().cpu(), vx.double().cpu(), do.double().cpu(), mask.cpu(),
+        block_m=128, block_n=128, is_causal=True, sink_size=S, window_size=W)
+    check_half(o, ro, dtype, "O")
+    check_half(dq, rdq, dtype, "dQ")
+    check_half(dk, rdk.sum(dim=1, keepdim=True), dtype, "dK")
+    check_half(dv, rdv.sum(dim=1, keepdim=True), dtype, "dV")
+    assert native.device_status() == 0
+
+
 def test_decode_custom_mask_and_noncausal():
     q, k, v, _ = _inputs(2, 3, 1, 640, 128, torch.float16, seed=7)
     mask = (torch.rand(1, 10, device=DEV) < 0.5).int()

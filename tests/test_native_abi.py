@@ -79,3 +79,14 @@ def test_last_error_truncates(lib):
     buf = ctypes.create_string_buffer(4)
     n = lib.sbfa_last_error(buf, 4)
     assert n > 3 and len(buf.value) == 3
+
+
+def test_bwd_workspace_bytes(lib):
+    """Split scratch is only needed with grouped K/V heads on the
+    tensor-core path: one fp32 [dV | dK] 128 x D partial per query head."""
+    assert lib.sbfa_bwd_workspace_bytes(4, 32, 128, native.BF16, 32) == 0
+    assert lib.sbfa_bwd_workspace_bytes(4, 32, 128, native.BF16, 0) == 0
+    assert lib.sbfa_bwd_workspace_bytes(4, 32, 128, native.BF16, 4) == 4 * 32 * 2 * 128 * 128 * 4
+    assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F16, 1) == 8 * 2 * 128 * 64 * 4
+    assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F32, 1) == 0
+    assert lib.sbfa_bwd_workspace_bytes(1, 8, 128, native.BF16, 3) == 0   # 8 % 3 != 0
