@@ -63,7 +63,7 @@ template <typename T, int DPL>
 __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     T* __restrict__ o, float* __restrict__ lse, int D, double scale_f, MaskParams mp, Views vw,
-    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, int* status) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   A* Qs = reinterpret_cast<A*>(smem_raw);   // [kRows][D]
@@ -87,9 +87,11 @@ __global__ void __launch_bounds__(kThreads) fwd_generic_kernel(
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[r][i] = 0;
   }
-  const int e0 = row_ptr[ti], e1 = row_ptr[ti + 1];
+  const int n_tj = ceil_div_dev(mp.n_kv, kKeys);  // key tiles (plan columns)
+  const PlanSpan span = plan_span(row_ptr, ti, n_tj, (int64_t)gridDim.x * n_tj, status);
+  const int e0 = span.e0, e1 = span.e0 + span.n;
   for (int e = e0; e < e1; ++e) {
-    const int32_t ent = col_idx[e];
+    const int32_t ent = plan_entry(col_idx, e, n_tj, status);
     const int tj = plan_index(ent);
     const bool partial = plan_partial(ent);
     const int k0 = tj * kKeys;
@@ -241,7 +243,8 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const T* __restrict__ dout, const float* __restrict__ lse,
     const float* __restrict__ delta, T* __restrict__ dq, int D, double scale_f, MaskParams mp,
-    Views vw, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+    Views vw, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+    int* status) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   A* Qs = reinterpret_cast<A*>(smem_raw);   // [kRows][D]
@@ -266,9 +269,11 @@ __global__ void __launch_bounds__(kThreads) dq_generic_kernel(
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[r][i] = 0;
   }
-  const int e0 = row_ptr[ti], e1 = row_ptr[ti + 1];
+  const int n_tj = ceil_div_dev(mp.n_kv, kKeys);  // key tiles (plan columns)
+  const PlanSpan span = plan_span(row_ptr, ti, n_tj, (int64_t)gridDim.x * n_tj, status);
+  const int e0 = span.e0, e1 = span.e0 + span.n;
   for (int e = e0; e < e1; ++e) {
-    const int32_t ent = col_idx[e];
+    const int32_t ent = plan_entry(col_idx, e, n_tj, status);
     const int tj = plan_index(ent);
     const bool partial = plan_partial(ent);
     const int k0 = tj * kKeys;
@@ -335,7 +340,7 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
     const T* __restrict__ dout, const float* __restrict__ lse,
     const float* __restrict__ delta, T* __restrict__ dk, T* __restrict__ dv, int D,
     double scale_f, MaskParams mp, Views vw, const int32_t* __restrict__ col_ptr,
-    const int32_t* __restrict__ row_idx) {
+    const int32_t* __restrict__ row_idx, int* status) {
   using A = typename Elem<T>::acc;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   A* Ks = reinterpret_cast<A*>(smem_raw);   // [kKvKeys][D]
@@ -360,12 +365,14 @@ __global__ void __launch_bounds__(kThreads) dkdv_generic_kernel(
   for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int i = 0; i < DPL; ++i) adk[c][i] = adv[c][i] = 0;
-  const int e0 = col_ptr[tj], ne = col_ptr[tj + 1] - e0;
+  const int n_ti = ceil_div_dev(mp.n_q, kKvRows);  // query tiles (plan rows)
+  const PlanSpan span = plan_span(col_ptr, tj, n_ti, (int64_t)n_ti * gridDim.x, status);
+  const int e0 = span.e0, ne = span.n;
   for (int it = 0; it < ne * vw.kv_group; ++it) {
     const int bh = bh0 + it / ne;
     const T* qb = q + vw.at(vw.q, bh, 0);
     const T* gb = dout + vw.at(vw.dout, bh, 0);
-    const int32_t ent = row_idx[e0 + it % ne];
+    const int32_t ent = plan_entry(row_idx, e0 + it % ne, n_ti, status);
     const int ti = plan_index(ent);
     const bool partial = plan_partial(ent);
     const int r0 = ti * kKvRows;
@@ -471,7 +478,7 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   {
     LaunchScope ls("fwd_generic_kernel", s);
     kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, D,
-                                    scale, mp, vw, row_ptr, col_idx);
+                                    scale, mp, vw, row_ptr, col_idx, device_status_ptr());
   }
   return check_launch("fwd_generic_kernel");
 }
@@ -492,7 +499,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
       LaunchScope ls("dkdv_generic_kernel", s);
       kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
                                       lse, delta, (T*)dk, (T*)dv, D, scale, mp, vw,
-                                      kv_col_ptr, kv_row_idx);
+                                      kv_col_ptr, kv_row_idx, device_status_ptr());
     }
     if (int rc = check_launch("dkdv_generic_kernel")) return rc;
   }
@@ -505,7 +512,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
       LaunchScope ls("dq_generic_kernel", s);
       kern<<<grid, kThreads, sm, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout,
                                       lse, delta, (T*)dq, D, scale, mp, vw, dq_row_ptr,
-                                      dq_col_idx);
+                                      dq_col_idx, device_status_ptr());
     }
     return check_launch("dq_generic_kernel");
   }

@@ -101,8 +101,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int bh = blockIdx.y;
   const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
   const int row0 = pair * kPair * kTM;
-  const int e0 = row_ptr[pair];
-  const int n = row_ptr[pair + 1] - e0;
+  const int n_tj = ceil_div_dev(mp.n_kv, kTN);  // key tiles (plan columns)
+  const PlanSpan span = plan_span(row_ptr, pair, n_tj, (int64_t)gridDim.x * n_tj, status);
+  const int e0 = span.e0;
+  const int n = span.n;
 
   if (n == 0) {  // no kept key tile: O = 0, LSE = 0 for every row of the pair
     for (int idx = threadIdx.x; idx < kPair * kTM * (D / 8); idx += blockDim.x) {
@@ -158,10 +160,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                       row0 + x * kTM, hh, bb);
       int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
       bool ok = true;
-      int next_ent = col_idx[e0];
+      int next_ent = plan_entry(col_idx, e0, n_tj, status);
       for (int j = 0; ok && j < n; ++j) {
         const int kt = plan_index(next_ent);
-        if (j + 1 < n) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
+        if (j + 1 < n) next_ent = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // prefetch
         for (int part = 0; part < 2; ++part) {
           const int e = 2 * j + part;
           const int s = e % STAGES, f = e / STAGES;
@@ -270,12 +272,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float m_run = -INFINITY, l_run = 0.f;
     bool settled = false;  // warp-uniform: every row of this warp has a finite running max
     bool ok = true;
-    int32_t ent = 0, ent_next = col_idx[e0];
+    int32_t ent = 0, ent_next = plan_entry(col_idx, e0, n_tj, status);
     for (int u = 0; u < U; ++u) {
       const int j = u >> 1, h = u & 1;
       if (h == 0) {
         ent = ent_next;
-        if (j + 1 < n) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
+        if (j + 1 < n) ent_next = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // in flight
       }
       const int k0 = plan_index(ent) * kTN + kHalf * h;
       const bool partial = plan_partial(ent);

@@ -159,8 +159,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   const int kv_heads = heads / kv_group;
   const int hh = bh % kv_heads, bb = bh / kv_heads;  // TMA coordinates of the K/V plane
-  const int e0 = col_ptr[tj];
-  const int nq = col_ptr[tj + 1] - e0;   // query tiles per query head
+  const int n_ti = ceil_div_dev(mp.n_q, kT);  // query tiles (plan rows)
+  const PlanSpan span = plan_span(col_ptr, tj, n_ti, (int64_t)n_ti * n_tj, status);
+  const int e0 = span.e0;
+  const int nq = span.n;                 // query tiles per query head
   // streamed tiles: tile i is query tile i % nq of query head
   // hh * kv_group + head_lo + i / nq
   const int ntot = nq * n_heads;
@@ -226,12 +228,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       int issued = 0;
-      int next_ent = row_idx[e0];
+      int next_ent = plan_entry(row_idx, e0, n_ti, status);
       bool ok = true;
       for (int i = 0; ok && i < ntot; ++i) {
         const int ti = plan_index(next_ent);
         const int hq = hh * kv_group + head_lo + i / nq;  // query head of tile i
-        if (i + 1 < ntot) next_ent = row_idx[e0 + (i + 1) % nq];  // prefetch the next entry
+        if (i + 1 < ntot)
+          next_ent = plan_entry(row_idx, e0 + (i + 1) % nq, n_ti, status);  // prefetch
         for (int part = 0; part < 2; ++part) {           // Q_i, then dO_i
           const int e = 2 * i + part, s = e % L::kRing, f = e / L::kRing;
           if (f > 0 && !wait_bar_w(bar(L::kREmpty + s), (uint32_t)((f - 1) & 1), abort_flag,
@@ -261,7 +264,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // tensor copies
       for (int i = 0; i < ntot; ++i) {
         const int slot = i & 1;
-        const int ti = plan_index(row_idx[e0 + i % nq]);
+        const int ti = plan_index(plan_entry(row_idx, e0 + i % nq, n_ti, status));
         const int row0 = ti * kT;
         const size_t qbh = (size_t)bb * heads + hh * kv_group + head_lo + i / nq;  // query (b, h)
         float lv[kT / 32], dv2[kT / 32];
@@ -361,13 +364,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int key = tj * kT + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
-    int32_t ent_next = row_idx[e0];
+    int32_t ent_next = plan_entry(row_idx, e0, n_ti, status);
     int pos_next = nq > 1 ? 1 : 0;  // (i + 1) % nq, kept as a counter (no division)
     for (int i = 0; i < ntot; ++i) {
       const int slot = i & 1;
       const uint32_t ph = (uint32_t)(i & 1);
       const int32_t ent = ent_next;
-      if (i + 1 < ntot) ent_next = row_idx[e0 + pos_next];  // in flight while this tile runs
+      if (i + 1 < ntot) ent_next = plan_entry(row_idx, e0 + pos_next, n_ti, status);  // in flight
       pos_next = pos_next + 1 == nq ? 0 : pos_next + 1;
       const int q0 = plan_index(ent) * kT + 64 * grp;
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
@@ -603,8 +606,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int ti = blockIdx.x;
   const int bh = blockIdx.y;
   const int hh = bh % heads, bb = bh / heads;  // TMA coordinates of the (batch, head) plane
-  const int e0 = row_ptr[ti];
-  const int nk = row_ptr[ti + 1] - e0;
+  const int n_tj = ceil_div_dev(mp.n_kv, kT);  // key tiles (plan columns)
+  const PlanSpan span = plan_span(row_ptr, ti, n_tj, (int64_t)gridDim.x * n_tj, status);
+  const int e0 = span.e0;
+  const int nk = span.n;
 
   if (nk == 0) {  // the tile's rows see no key: dQ = 0
     for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
@@ -652,11 +657,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
       }
       int fills[kRing] = {};  // copies issued per ring slot
-      int next_ent = col_idx[e0];
+      int next_ent = plan_entry(col_idx, e0, n_tj, status);
       bool ok = true;
       for (int j = 0; ok && j < nk; ++j) {
         const int kt = plan_index(next_ent);
-        if (j + 1 < nk) next_ent = col_idx[e0 + j + 1];  // prefetch the next plan entry
+        if (j + 1 < nk) next_ent = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // prefetch
         // K_j (entry 2j+1) before V_j (entry 2j): K_j is read first (by S(j),
         // issued a tile before dP(j)), and its slot was freed earlier (by
         // V_{j-2}, released as soon as dP(j-2) was issued).  Each slot is still
@@ -762,10 +767,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = in ? lse[(size_t)bh * mp.n_q + row] * kLog2e : 0.f;
     const float dl = in ? delta[(size_t)bh * mp.n_q + row] : 0.f;
     bool ok = true;
-    int32_t ent_next = col_idx[e0];
+    int32_t ent_next = plan_entry(col_idx, e0, n_tj, status);
     for (int j = 0; j < nk; ++j) {
       const int32_t ent = ent_next;
-      if (j + 1 < nk) ent_next = col_idx[e0 + j + 1];  // in flight while this tile runs
+      if (j + 1 < nk) ent_next = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // in flight
       const int k0 = plan_index(ent) * kT + 64 * grp;
       uint32_t vis[2] = {0xffffffffu, 0xffffffffu};
       const bool all_vis = block_all_visible(mp, ti * kT, kT, k0, 64, plan_partial(ent));

@@ -79,9 +79,15 @@ struct PlanKeys {
   MaskParams mp;
   const int32_t* row_ptr;
   const int32_t* col_idx;
-  __device__ __forceinline__ int total() const { return (row_ptr[1] - row_ptr[0]) * kDecTile; }
+  int* status;  // debug builds record out-of-range plan indices here
+  __device__ __forceinline__ PlanSpan span() const {
+    const int n_tiles = ceil_div_dev(mp.n_kv, kDecTile);
+    return plan_span(row_ptr, 0, n_tiles, n_tiles, status);
+  }
+  __device__ __forceinline__ int total() const { return span().n * kDecTile; }
   __device__ __forceinline__ bool key(int t, int* row) const {
-    const int32_t ent = col_idx[row_ptr[0] + t / kDecTile];
+    const int32_t ent =
+        plan_entry(col_idx, span().e0 + t / kDecTile, ceil_div_dev(mp.n_kv, kDecTile), status);
     const int kk = plan_index(ent) * kDecTile + (t % kDecTile);
     *row = kk;
     return visible(mp, 0, kk, plan_partial(ent));
@@ -454,7 +460,7 @@ int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit) {
 int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
                const int32_t* ci, int nsplit, int heads, int group, cudaStream_t s) {
-  const PlanKeys keys{mp, rp, ci};
+  const PlanKeys keys{mp, rp, ci, device_status_ptr()};
   return decode_any(dtype, q, k, v, o, lse, ws, BH, D, scale, keys, (int64_t)mp.n_kv, nsplit,
                     heads, group, s);
 }

@@ -129,11 +129,70 @@ int* device_status_ptr();
 // Status codes a kernel may record (first writer wins).
 constexpr int kStatusWaitTimeout = 1;
 constexpr int kStatusBadSmemAlign = 2;
+constexpr int kStatusBoundsCheck = 3;  // debug builds: an index was out of range
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// ---------------------------------------------------------------------------
+// Bounds checks of the debug build (compiled with SBFA_DEBUG_BOUNDS)
+// ---------------------------------------------------------------------------
+// Every index a kernel reads from a plan (list offsets, list lengths, tile
+// indices) and the tile coordinates derived from it go through these.  In
+// the debug build a value outside its range is recorded in the status word
+// (kStatusBoundsCheck) and replaced by the nearest value in range, so the
+// access it feeds stays inside its buffer and no pipeline changes shape; in
+// release builds they return the value unchanged.
+__device__ __forceinline__ int bounded(int v, int hi, int* status) {
+#ifdef SBFA_DEBUG_BOUNDS
+  if (v < 0 || v >= hi) {
+    record_status(status, kStatusBoundsCheck);
+    return v < 0 ? 0 : max(hi - 1, 0);
+  }
+#endif
+  (void)hi;
+  (void)status;
+  return v;
+}
+
+// The list [e0, e0 + n) of line i of a compacted plan (CSR row_ptr or CSC
+// col_ptr): e0 within the cap entries of the list array, n within the
+// n_other tiles of the crossing dimension and the array's end.
+struct PlanSpan {
+  int e0, n;
+};
+__device__ __forceinline__ PlanSpan plan_span(const int32_t* ptr, int i, int n_other,
+                                              int64_t cap, int* status) {
+  PlanSpan s{ptr[i], ptr[i + 1] - ptr[i]};
+#ifdef SBFA_DEBUG_BOUNDS
+  const int icap = (int)min(cap, (int64_t)0x7fffffff - 1);
+  s.e0 = bounded(s.e0, icap + 1, status);
+  s.n = bounded(s.n, min(n_other, icap - s.e0) + 1, status);
+#endif
+  (void)n_other;
+  (void)cap;
+  return s;
+}
+
+// Plan entry e of a list: tile index checked against the n_other tiles of
+// the crossing dimension, the partial bit kept.
+__device__ __forceinline__ int32_t plan_entry(const int32_t* list, int e, int n_other,
+                                              int* status) {
+  const int32_t ent = list[e];
+#ifdef SBFA_DEBUG_BOUNDS
+  const int idx = bounded((int)((uint32_t)ent & 0x7fffffffu), n_other, status);
+  return (int32_t)(((uint32_t)ent & 0x80000000u) | (uint32_t)idx);
+#else
+  (void)n_other;
+  (void)status;
+  return ent;
+#endif
+}
+
 inline int ceil_div_i(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+__device__ __forceinline__ int ceil_div_dev(int a, int b) {
+  return (int)(((int64_t)a + b - 1) / b);
+}
 
 // Wraps one kernel launch: counts it, and when timing is enabled
 // (sbfa_timing_enable) records a CUDA event pair around it on its stream,

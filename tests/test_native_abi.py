@@ -90,3 +90,15 @@ def test_bwd_workspace_bytes(lib):
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F16, 1) == 8 * 2 * 128 * 64 * 4
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F32, 1) == 0
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 128, native.BF16, 3) == 0   # 8 % 3 != 0
+
+
+def test_debug_library_exports_the_same_symbols():
+    """libsbfa_debug.so (device-side bounds checks) is a drop-in build of the
+    same ABI."""
+    path = os.path.join(os.path.dirname(native.LIB_PATH), "libsbfa_debug.so")
+    if not os.path.exists(path):
+        pytest.fail("libsbfa_debug.so is not built (run __graft_entry__.build())")
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (sbfa_[a-z0-9_]+)", out))
+    assert set(declared_functions()) <= exported
