@@ -463,6 +463,8 @@ def bench_fwdbwd(dist, args, pk, src):
         "d2h_bytes_per_step": bytes_d2h * dist.world,
         "ms_per_step": round(e_ms / e_steps, 3),
         "pipeline": "copy-in / compute / copy-out on three streams, two steps in flight"}
+    if e2e is not None:
+        e2e["copies"] = copy_peaks(dist, host_in, dev_in[0], out_h[0], e_ms / e_steps)
     del dev_in, hq, hk, hv, hdo, host_in, out_h
     rl = roofline(per_kernel, F_local, pk, src, clocks=clk, workload="cfg2",
                   scale_units=(stop - start) / units)
@@ -474,6 +476,46 @@ def bench_fwdbwd(dist, args, pk, src):
     if dist.world > 1 and not args.no_weak:
         res["weak"] = bench_fwdbwd_weak(dist, args, F)
     return res
+
+
+def copy_peaks(dist, host_in, dev_bufs, host_out, step_ms):
+    """Pinned host<->device copy bandwidth of this rank's e2e tensors, each
+    direction alone and both at once (the pipelined step overlaps them), and
+    the copy-bound floor of one e2e step it implies (max over ranks)."""
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    nbytes_in = sum(t.numel() * t.element_size() for t in host_in)
+    nbytes_out = sum(t.numel() * t.element_size() for t in host_out)
+
+    def timed(h2d: bool, d2h: bool, reps: int = 2) -> float:
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for st in (s_in, s_out):
+            st.wait_event(a)
+        for _ in range(reps):
+            if h2d:
+                with torch.cuda.stream(s_in):
+                    for d, h in zip(dev_bufs, host_in):
+                        d.copy_(h, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s_out):
+                    for h, d in zip(host_out, dev_bufs):
+                        h.copy_(d, non_blocking=True)
+        cur = torch.cuda.current_stream()
+        for st in (s_in, s_out):
+            cur.wait_stream(st)
+        b.record()
+        torch.cuda.synchronize()
+        return dist.max(a.elapsed_time(b) / reps)
+
+    h2d_ms, d2h_ms, both_ms = timed(True, False), timed(False, True), timed(True, True)
+    return {"h2d_gbs": round(nbytes_in / h2d_ms / 1e6, 1),
+            "d2h_gbs": round(nbytes_out / d2h_ms / 1e6, 1),
+            "both_directions_ms": round(both_ms, 3),
+            "copy_bound_fraction": round(both_ms / step_ms, 3),
+            "note": "pinned copies of the step's own tensors, per rank; copy_bound_fraction ="
+                    " both-direction copy time / e2e step time"}
 
 
 def bench_fwdbwd_weak(dist, args, F):
