@@ -139,6 +139,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(bar(L::kDrain + 1), 1);
     *abort_flag = 0;
     mbar_init_fence();
+    // the resident Q_A, Q_B tiles are requested before the TMEM allocation
+    // and the CTA-wide sync, so their latency overlaps them
+    mbar_expect_tx(bar(L::kQFull), kPair * L::kTile);
+    for (int x = 0; x < kPair; ++x)
+      for (int r = 0; r < kBoxes; ++r)
+        tma_load_4d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
+                    row0 + x * kTM, hh, bb);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -153,11 +160,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
    regs_dec<kRegsCtl>();
    if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
-      mbar_expect_tx(bar(L::kQFull), kPair * L::kTile);
-      for (int x = 0; x < kPair; ++x)
-        for (int r = 0; r < kBoxes; ++r)
-          tma_load_4d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
-                      row0 + x * kTM, hh, bb);
+      // (Q_A, Q_B were requested by this thread right after the barrier set-up)
       int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
       bool ok = true;
       int next_ent = plan_entry(col_idx, e0, n_tj, status);

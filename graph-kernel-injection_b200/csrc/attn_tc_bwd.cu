@@ -206,6 +206,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
     mbar_init_fence();
+    // the resident K, V tiles are requested before the TMEM allocation and
+    // the CTA-wide sync, so their latency overlaps them
+    mbar_expect_tx(bar(L::kKVFull), 2 * L::kTile);
+    for (int r = 0; r < kBoxes; ++r) {
+      tma_load_4d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
+      tma_load_4d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -220,13 +227,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     regs_dec<kRegsCtl>();
     if (warp == 0) {
       // ---------------------------------------------------------- producer
-      if (lane == 0) {
-        mbar_expect_tx(bar(L::kKVFull), 2 * L::kTile);
-        for (int r = 0; r < kBoxes; ++r) {
-          tma_load_4d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
-          tma_load_4d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
-        }
-      }
+      // (K, V were requested by this thread right after the barrier set-up)
       int issued = 0;
       int next_ent = plan_entry(row_idx, e0, n_ti, status);
       bool ok = true;
@@ -637,6 +638,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
     mbar_init_fence();
+    // the resident Q, dO tiles are requested before the TMEM allocation and
+    // the CTA-wide sync, so their latency overlaps them
+    mbar_expect_tx(bar(L::kQFull), 2 * L::kTile);
+    for (int r = 0; r < kBoxes; ++r) {
+      tma_load_4d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
+      tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -651,11 +659,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     regs_dec<kRegsCtl>();
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------- producer
-      mbar_expect_tx(bar(L::kQFull), 2 * L::kTile);
-      for (int r = 0; r < kBoxes; ++r) {
-        tma_load_4d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
-        tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
-      }
+      // (Q, dO were requested by this thread right after the barrier set-up)
       int fills[kRing] = {};  // copies issued per ring slot
       int next_ent = plan_entry(col_idx, e0, n_tj, status);
       bool ok = true;
