@@ -146,6 +146,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int r = 0; r < kBoxes; ++r)
         tma_load_4d(sb + L::Q + x * L::kTile + r * 16384u, &tmq, bar(L::kQFull), 64 * r,
                     row0 + x * kTM, hh, bb);
+    // ... and so are the first ring entries, K_0 and V_0 (fresh slots 0, 1)
+    const int kt0 = plan_index(plan_entry(col_idx, e0, n_tj, status));
+    for (int part = 0; part < 2; ++part) {
+      mbar_expect_tx(bar(L::kKVFull + part), L::kTile);
+      for (int r = 0; r < kBoxes; ++r)
+        tma_load_4d(sb + L::KV + part * L::kTile + r * 16384u, part == 0 ? &tmk : &tmv,
+                    bar(L::kKVFull + part), 64 * r, kt0 * kTN, hh / kv_group, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -160,11 +168,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
    regs_dec<kRegsCtl>();
    if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
-      // (Q_A, Q_B were requested by this thread right after the barrier set-up)
-      int issued = 0;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
+      // (Q_A, Q_B, K_0 and V_0 were requested by this thread right after the
+      // barrier set-up)
+      int issued = 2;  // ring entries issued: entry 2j = K_j, 2j + 1 = V_j
       bool ok = true;
-      int next_ent = plan_entry(col_idx, e0, n_tj, status);
-      for (int j = 0; ok && j < n; ++j) {
+      int next_ent = n > 1 ? plan_entry(col_idx, e0 + 1, n_tj, status) : 0;
+      for (int j = 1; ok && j < n; ++j) {
         const int kt = plan_index(next_ent);
         if (j + 1 < n) next_ent = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // prefetch
         for (int part = 0; part < 2; ++part) {

@@ -213,6 +213,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_load_4d(sb + L::K + r * 16384u, &tmk, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
       tma_load_4d(sb + L::V + r * 16384u, &tmv, bar(L::kKVFull), 64 * r, tj * kT, hh, bb);
     }
+    // ... and so are the first ring entries, Q_0 and dO_0 (fresh slots 0, 1)
+    const int ti0 = plan_index(plan_entry(row_idx, e0, n_ti, status));
+    for (int part = 0; part < 2; ++part) {
+      mbar_expect_tx(bar(L::kRFull + part), L::kTile);
+      for (int r = 0; r < kBoxes; ++r)
+        tma_load_4d(sb + L::RING + part * L::kTile + r * 16384u, part ? &tmdo : &tmq,
+                    bar(L::kRFull + part), 64 * r, ti0 * kT, hh * kv_group + head_lo, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -227,11 +235,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     regs_dec<kRegsCtl>();
     if (warp == 0) {
       // ---------------------------------------------------------- producer
-      // (K, V were requested by this thread right after the barrier set-up)
-      int issued = 0;
-      int next_ent = plan_entry(row_idx, e0, n_ti, status);
+      // (K, V, Q_0 and dO_0 were requested by this thread right after the
+      // barrier set-up)
+      int issued = 2;
+      int next_ent = ntot > 1 ? plan_entry(row_idx, e0 + (1 % nq), n_ti, status) : 0;
       bool ok = true;
-      for (int i = 0; ok && i < ntot; ++i) {
+      for (int i = 1; ok && i < ntot; ++i) {
         const int ti = plan_index(next_ent);
         const int hq = hh * kv_group + head_lo + i / nq;  // query head of tile i
         if (i + 1 < ntot)
@@ -645,6 +654,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_load_4d(sb + L::Q + r * 16384u, &tmq, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
       tma_load_4d(sb + L::DO + r * 16384u, &tmdo, bar(L::kQFull), 64 * r, ti * kT, hh, bb);
     }
+    // ... and so are the first ring entries, K_0 (entry 1) and V_0 (entry 0)
+    const int kt0 = plan_index(plan_entry(col_idx, e0, n_tj, status));
+    for (int part = 1; part >= 0; --part) {
+      mbar_expect_tx(bar(L::kRFull + part), L::kTile);
+      for (int r = 0; r < kBoxes; ++r)
+        tma_load_4d(sb + L::RING + part * L::kTile + r * 16384u, part ? &tmk : &tmv,
+                    bar(L::kRFull + part), 64 * r, kt0 * kT, hh / kv_group, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -659,11 +676,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     regs_dec<kRegsCtl>();
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------- producer
-      // (Q, dO were requested by this thread right after the barrier set-up)
-      int fills[kRing] = {};  // copies issued per ring slot
-      int next_ent = plan_entry(col_idx, e0, n_tj, status);
+      // (Q, dO, K_0 and V_0 were requested by this thread right after the
+      // barrier set-up)
+      int fills[kRing] = {1, 1};  // copies issued per ring slot
+      int next_ent = nk > 1 ? plan_entry(col_idx, e0 + 1, n_tj, status) : 0;
       bool ok = true;
-      for (int j = 0; ok && j < nk; ++j) {
+      for (int j = 1; ok && j < nk; ++j) {
         const int kt = plan_index(next_ent);
         if (j + 1 < nk) next_ent = plan_entry(col_idx, e0 + j + 1, n_tj, status);  // prefetch
         // K_j (entry 2j+1) before V_j (entry 2j): K_j is read first (by S(j),
