@@ -189,7 +189,7 @@ def kernel_kind(name: str):
     for kind in ("dkdv", "dq", "fwd"):
         if name.startswith(kind):
             return kind
-    if name.startswith("decode_split"):
+    if name.startswith(("decode_split", "decode_gqa")):
         return "decode"
     return None
 
@@ -808,6 +808,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
                     help="override the head count of configs 2-4 (small cases for profiling)")
+    ap.add_argument("--decode-n-kv", type=int, default=0,
+                    help="override config 4's cache length (small cases for profiling: the "
+                         "visible rows per step, hence the traffic and grid, stay the same "
+                         "while N_KV > S + W)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-weak", action="store_true",
                     help="skip the weak-scaling reference leg (N > 1)")
@@ -817,6 +821,8 @@ def main():
     if args.heads > 0:
         for cfg in (CFG2, CFG3, CFG4):
             cfg["H"] = args.heads
+    if args.decode_n_kv > 0:
+        CFG4["N"] = args.decode_n_kv
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -860,7 +866,7 @@ def main():
         r = bench_decode(dist, args, pk, src)
         extra["cfg4_decode"] = {"value": round(r["value"], 2), "unit": "GB/s",
                                 "ms_per_step": round(r["ms"], 4), "roofline": r["roofline"],
-                                "kv_bytes_per_step": r["kv_bytes"],
+                                "kv_bytes_per_step": r["kv_bytes"], "n_kv": CFG4["N"],
                                 "gpu_launches": r["launches"], "units_rank0": list(r["units"][:2])}
         extra["cfg4_decode_ring_cache"] = r["ring"]
         extra["cfg4_decode_gqa"] = r["gqa"]

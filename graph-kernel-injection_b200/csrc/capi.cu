@@ -28,9 +28,9 @@ int generic_bwd(int dtype, int D, const void* q, const void* k, const void* v, c
 int decode_tile();
 int64_t decode_est_tiles(int64_t n_kv, int is_causal, int64_t sink, int64_t window);
 int decode_group(int dtype, int64_t D);
-int decode_nsplit(int64_t BH, int64_t est_tiles);
+int decode_splits(int64_t BH, int group, int dtype, int64_t D, int64_t est_tiles);
+int decode_max_splits(int64_t BH, int64_t est_tiles);
 int64_t decode_ws_bytes(int64_t BH, int64_t D, int nsplit);
-int decode_heads_per_cta(int group);
 int decode_run(int dtype, const void* q, const void* k, const void* v, void* o, float* lse,
                void* ws, int BH, int D, float scale, const MaskParams& mp, const int32_t* rp,
                const int32_t* ci, int nsplit, int heads, int group, cudaStream_t s);
@@ -420,8 +420,7 @@ extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_k
   // and over head groupings (the most query heads per CTA, so the fewest
   // CTAs per split and the most splits)
   if (B <= 0 || H <= 0 || head_dim <= 0 || n_kv <= 0) return 0;
-  const int64_t ctas = std::max<int64_t>(1, B * H / decode_heads_per_cta(1 << 30));
-  const int ns = decode_nsplit(ctas, decode_est_tiles(n_kv, 0, 0, 0));
+  const int ns = decode_max_splits(B * H, decode_est_tiles(n_kv, 0, 0, 0));
   return decode_ws_bytes(B * H, head_dim, ns);
 }
 
@@ -437,7 +436,7 @@ extern "C" int sbfa_decode(const void* q, const void* k, const void* v, void* o,
   if (!row_ptr || !col_idx) return fail(SBFA_ERR_INVALID, "sbfa_decode: NULL plan pointer");
   if (kv_heads <= 0) kv_heads = H;
   const int group = (int)(H / kv_heads);
-  const int ns = decode_nsplit(B * H / decode_heads_per_cta(group),
+  const int ns = decode_splits(B * H, group, dtype, head_dim,
                                decode_est_tiles(n_kv, is_causal, sink, window));
   const int64_t need = decode_ws_bytes(B * H, head_dim, ns);
   if (need > 0 && (split_ws == nullptr || split_ws_bytes < need))

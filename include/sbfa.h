@@ -199,8 +199,10 @@ int64_t sbfa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t head_dim, int dty
  * Reads only the K/V rows the query can see.  row_ptr/col_idx: plan of
  * pass 3.  split_ws: caller scratch of sbfa_decode_workspace_bytes() bytes.
  * lse may be NULL.  q, o: contiguous [B, H, 1, D]; k, v: contiguous
- * [B, kv_heads, n_kv, D] (kv_heads <= 0 means H); with kv_heads < H each
- * K/V row is read once for all the query heads of its group. */
+ * [B, kv_heads, n_kv, D] (kv_heads <= 0 means H).  With kv_heads < H a CTA
+ * serves several query heads of one K/V head, so each K/V row is read once
+ * per 16 query heads of its group (fp16/bf16 with head_dim 64 or 128, on the
+ * tensor cores) or per 4 (other dtypes and head dims). */
 int sbfa_decode(const void* q, const void* k, const void* v, void* o, float* lse,
                 int64_t B, int64_t H, int64_t n_kv, int64_t head_dim, int dtype,
                 double softmax_scale, int is_causal, int64_t sink, int64_t window,

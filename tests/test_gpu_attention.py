@@ -233,11 +233,15 @@ def test_decode_matches_oracle(case):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("H,Hkv,n_kv,D", [(8, 2, 3000, 128), (8, 1, 2500, 128),
-                                          (6, 2, 1777, 64), (32, 4, 4100, 128)])
+                                          (6, 2, 1777, 64), (32, 4, 4100, 128),
+                                          (32, 1, 1500, 128), (20, 1, 700, 64),
+                                          (4, 2, 50, 128)])
 def test_grouped_query_decode(dtype, H, Hkv, n_kv, D):
-    """N_Q = 1 with fewer K/V heads than query heads runs the split-KV decode
-    kernel (each K/V row read once for the query heads of its group; groups
-    of 4, 8 and 3), against the float64 oracle per query head."""
+    """N_Q = 1 with fewer K/V heads than query heads runs the tensor-core
+    grouped decode kernel (each K/V row read once for up to 16 query heads
+    of its group; groups of 2, 3, 4, 8, 20 (two CTAs of 10) and 32 (two of
+    16); a 50-key cache in one tile, hence one split), against the float64
+    oracle per query head."""
     B, S, W = 2, 4, 1024
     g = torch.Generator(device=DEV).manual_seed(31)
     q = torch.randn(B, H, 1, D, generator=g, device=DEV, dtype=dtype)
@@ -253,7 +257,8 @@ def test_grouped_query_decode(dtype, H, Hkv, n_kv, D):
         ran = native.timing_read()
     finally:
         native.timing(False)
-    assert "decode_split_kernel" in ran and not any(n.startswith("fwd") for n in ran), ran
+    assert "decode_gqa_kernel" in ran, ran
+    assert "decode_split_kernel" not in ran and not any(n.startswith("fwd") for n in ran), ran
     scale = 1 / math.sqrt(D)
     grp = H // Hkv
     for b in range(B):
@@ -315,6 +320,48 @@ def test_decode_custom_mask_and_noncausal():
                                    mask.cpu(), block_m=1, block_n=64, is_causal=causal,
                                    sink_size=4, window_size=100)
         close(o, ro, torch.float16)
+
+
+@pytest.mark.parametrize("dtype,D,H,Hkv,bn", [(torch.bfloat16, 128, 8, 2, 32),
+                                              (torch.float16, 64, 12, 3, 64)])
+def test_grouped_query_decode_custom_mask_and_grad(dtype, D, H, Hkv, bn):
+    """The tensor-core grouped decode under a random block mask (with 32-key
+    mask blocks the 64-key decode tiles are partly kept), causal and not,
+    against the oracle on K/V repeated per group; with gradients, its LSE
+    feeds the backward, checked the same way."""
+    B, n_kv, S, W = 2, 777, 4, 200
+    gen = torch.Generator(device=DEV).manual_seed(41)
+    q = torch.randn(B, H, 1, D, generator=gen, device=DEV, dtype=dtype)
+    k = torch.randn(B, Hkv, n_kv, D, generator=gen, device=DEV, dtype=dtype)
+    v = torch.randn(B, Hkv, n_kv, D, generator=gen, device=DEV, dtype=dtype)
+    do = torch.randn(B, H, 1, D, generator=gen, device=DEV, dtype=dtype)
+    n_kb = (n_kv + bn - 1) // bn
+    mask = (torch.rand(1, n_kb, generator=gen, device=DEV) < 0.5).int()
+    mask[0, 0] = mask[0, -1] = 1
+    rep = H // Hkv
+    ke, ve = (t.repeat_interleave(rep, dim=1) for t in (k, v))
+    for causal in (False, True):
+        native.timing_read()
+        native.timing(True)
+        try:
+            o, dq, dk, dv = run(q, k, v, mask, 1, bn, causal, S, W, do=do)
+            ran = native.timing_read()
+        finally:
+            native.timing(False)
+        assert "decode_gqa_kernel" in ran, ran
+        ro, rdq, rdk, rdv = orc.attention_forward_backward(
+            q.double().cpu(), ke.double().cpu(), ve.double().cpu(), do.double().cpu(),
+            mask.cpu(), block_m=1, block_n=bn, is_causal=causal, sink_size=S, window_size=W)
+        rdk = rdk.view(B, Hkv, rep, n_kv, D).sum(2)
+        rdv = rdv.view(B, Hkv, rep, n_kv, D).sum(2)
+        check_half(o, ro, dtype, f"gqa decode causal={causal} O")
+        check_half(dq, rdq, dtype, f"gqa decode causal={causal} dQ")
+        check_half(dk, rdk, dtype, f"gqa decode causal={causal} dK")
+        check_half(dv, rdv, dtype, f"gqa decode causal={causal} dV")
+    # no kept block: every head's output is 0 (upstream's empty-row rule)
+    o, *_ = run(q, k, v, torch.zeros_like(mask), 1, bn, False, S, W)
+    assert torch.equal(o, torch.zeros_like(o))
+    assert native.device_status() == 0
 
 
 def test_decode_backward_runs_generic_path():
