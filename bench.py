@@ -263,16 +263,17 @@ def roofline(per_kernel, flops_fwd, pk, peak_src, clocks=None, kv_bytes=None, wo
                              for k, v in per_kernel.items()}}
 
 
-def executed_mma_flops(mask, cfg, units):
+def executed_mma_flops(mask, cfg, units, dq_gemms=3):
     """Tensor-core FLOPs each kernel issues per step for `units` (batch,
     head) pairs, from the kept tiles of the plans the kernels walk (the
     forward's 256-row query-pair tiles visit the union of both tiles' kept
-    key tiles; the dQ kernel recomputes S and dP), next to the algorithmic
-    FLOPs of the same launch."""
+    key tiles; the recomputing dQ kernel issues S, dP and dQ, the dQ GEMM
+    over stored dS only dQ), next to the algorithmic FLOPs of the same
+    launch."""
     import sparse_triton_kernel as stk
     D, N, dt = cfg["D"], cfg["N"], cfg["dtype"]
     out = {}
-    for kind, pass_id, gemms in (("fwd", 0, 2), ("dkdv", 2, 4), ("dq", 1, 3)):
+    for kind, pass_id, gemms in (("fwd", 0, 2), ("dkdv", 2, 4), ("dq", 1, dq_gemms)):
         p = stk._plan_for(mask, pass_id, dt, D, N, N, cfg["BM"], cfg["BN"])
         tm, tn = p["tiles"]
         tiles = int(p["nnz"].item())
@@ -846,7 +847,8 @@ def main():
                            "verify_rank0": r["verify"],
                            "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()}}
         _, mask = kept_blocks(CFG2)
-        ex = executed_mma_flops(mask, CFG2, stop - start)
+        ex = executed_mma_flops(mask, CFG2, stop - start,
+                                dq_gemms=1 if "dq_gemm_kernel" in r["per_kernel"] else 3)
         alg = {k: KERNEL_WORK[k] * r["flops_fwd"] * (stop - start) / units for k in ex}
         extra["fwdbwd"]["mma_flops_per_launch_rank0"] = {
             k: {"executed": ex[k], "algorithmic": alg[k], "ratio": round(ex[k] / alg[k], 4)}

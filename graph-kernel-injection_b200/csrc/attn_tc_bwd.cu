@@ -67,16 +67,24 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
 // Streamed tiles share one ring of kRing entries, entry 2i = Q_i and
 // 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
 // dK once in the epilogue.
-template <int D>
+//
+// With DS the kernel also stores every dS_i^T tile (128 keys x 128 queries,
+// 16-bit) to global memory for dq_gemm_kernel: each compute thread writes its
+// key's 64 columns into a swizzled shared-memory staging tile and warp 3
+// writes the tile out with two TMA stores, at the CSC position of the
+// (query head, key tile, query tile) triple.
+template <int D, bool DS = false>
 struct DkdvLayout {
   // K, V and a 5-entry ring of 128-column tiles fill 224 KB; 64-column
-  // tiles leave room for 6 ring entries
-  static constexpr int kRing = D > 64 ? 5 : 6;
+  // tiles leave room for 6 ring entries.  With DS the 32 KB dS staging tile
+  // takes one 128-column ring entry.
+  static constexpr int kRing = D > 64 ? (DS ? 4 : 5) : 6;
   static constexpr uint32_t kTile = kT * D * 2;
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + kTile;
   static constexpr uint32_t RING = V + kTile;               // kRing streamed tiles
-  static constexpr uint32_t LS = RING + kRing * kTile;       // 2 x 128 floats (LSE * log2 e)
+  static constexpr uint32_t DSB = RING + kRing * kTile;      // dS^T staging (DS only)
+  static constexpr uint32_t LS = DSB + (DS ? 2u * 16384u : 0u);  // 2 x 128 floats (LSE * log2 e)
   static constexpr uint32_t DL = LS + 2 * kT * 4;            // 2 x 128 floats (Delta)
   static constexpr uint32_t BAR = DL + 2 * kT * 4;
   static constexpr int kKVFull = 0;
@@ -90,7 +98,9 @@ struct DkdvLayout {
   static constexpr int kDSReady = 8 + 2 * kRing;     // P_i and dS_i packed in TMEM
   static constexpr int kDone = 9 + 2 * kRing;
   static constexpr int kDrain = 10 + 2 * kRing;
-  static constexpr int kNumBars = 11 + 2 * kRing;
+  static constexpr int kStageFull = 11 + 2 * kRing;  // dS_i staged (DS)
+  static constexpr int kStageFree = 12 + 2 * kRing;  // staging read by the TMA store (DS)
+  static constexpr int kNumBars = 13 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kBytes = MISC + 16;
   // D = 128 leaves no room to align the window by hand: the kernel checks
@@ -100,18 +110,19 @@ struct DkdvLayout {
   static constexpr uint32_t kAlloc = kAlignInKernel ? kBytes + 1024 : kBytes;
 };
 
-template <typename T, int D>
+template <typename T, int D, bool DS>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
                    const __grid_constant__ CUtensorMap tmdk,
-                   const __grid_constant__ CUtensorMap tmdv, T* __restrict__ dk,
+                   const __grid_constant__ CUtensorMap tmdv,
+                   T* __restrict__ ds, int nnz, T* __restrict__ dk,
                    T* __restrict__ dv, const float* __restrict__ lse,
                    const float* __restrict__ delta, float scale, float scale_log2, MaskParams mp,
                    const int32_t* __restrict__ col_ptr, const int32_t* __restrict__ row_idx, int BH,
                    int n_tj, int heads, int kv_group, Strides3 sdk, Strides3 sdv,
                    float* __restrict__ part_ws, int sink_parts, int* status) {
-  using L = DkdvLayout<D>;
+  using L = DkdvLayout<D, DS>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBF16, kT, kT, false, false);   // M=128 keys, N=128 q
   constexpr uint32_t kIdescAcc = idesc_f16(kBF16, kT, D, false, true);   // M=128 keys, N=D
@@ -204,6 +215,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
+    if (DS) {
+      mbar_init(bar(L::kStageFull), 256);
+      mbar_init(bar(L::kStageFree), 1);
+    }
     *abort_flag = 0;
     mbar_init_fence();
     // the resident K, V tiles are requested before the TMEM allocation and
@@ -297,6 +312,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::kLFull + slot));
+      }
+    } else if (DS && warp == 3) {
+      // ------------------------------------------------------ dS^T store
+      // tile i of this CTA: query head hh * kv_group + head_lo + i / nq, CSC
+      // entry e0 + i % nq; stored as tile (query (b, h)) * nnz + entry
+      for (int i = 0; i < ntot; ++i) {
+        if (!wait_bar_w(bar(L::kStageFull), (uint32_t)(i & 1), abort_flag, status)) break;
+        if (lane == 0) {
+          const int hq = hh * kv_group + head_lo + i / nq;
+          const int tile = (bb * heads + hq) * nnz + e0 + i % nq;
+          bulk_store(ds + (size_t)tile * (kT * kT), sb + L::DSB, 2u * 16384u);
+          bulk_commit();
+          bulk_wait_read0();
+          mbar_arrive(bar(L::kStageFree));
+        }
+        __syncwarp();
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
@@ -458,6 +489,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(L::kDSReady));
+      if constexpr (DS) {
+        // this key's row of dS_i^T, query columns [64g, 64g+64), into the
+        // staging tile once the store of dS_{i-1} has read it
+        if (i > 0 &&
+            !wait_bar_w(bar(L::kStageFree), (uint32_t)((i - 1) & 1), abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        const uint32_t region = sb + L::DSB + (uint32_t)grp * 16384u;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t addr = region + sw128_offset((uint32_t)r, 8u * c);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(dsk[4 * c]),
+                       "r"(dsk[4 * c + 1]), "r"(dsk[4 * c + 2]), "r"(dsk[4 * c + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bar(L::kStageFull));
+      }
     }
     // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes
     // dK * scale (staged in V's buffer); both buffers are free once every
@@ -887,12 +937,202 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// dQ from stored dS (after dkdv_tc_kernel<..., DS = true>)
+// ---------------------------------------------------------------------------
+// dQ_i = scale * sum_j dS_ij K_j over the key tiles j query tile i sees (CSR
+// plan), with dS_ij^T read from the tile dkdv_tc_kernel stored at
+// (query (b, h)) * nnz + csc_pos[p] for CSR entry p.  One CTA per (query
+// tile, query (b, h)): warp 0 streams (dS_ij^T, K_j) pairs through a ring
+// with TMA, warp 1 issues 128 x D x 128 MMAs (A = dS_ij, M-major from the
+// stored [key][query] tile; B = K_j, N-major) into a TMEM accumulator, and
+// the four warps write dQ (one query row per thread) through a TMA store.
+// No exponentials, no recomputed S or dP: the kernel moves 32 KB of dS per
+// kept tile and is bound by HBM.
+template <int D>
+struct DqGemmLayout {
+  static constexpr int kStages = D > 64 ? 3 : 4;
+  static constexpr uint32_t kDsTile = kT * kT * 2;   // dS^T [128 keys][128 queries]
+  static constexpr uint32_t kKTile = kT * D * 2;     // K_j [128 keys][D]
+  static constexpr uint32_t kStage = kDsTile + kKTile;
+  static constexpr uint32_t RING = 0;
+  static constexpr uint32_t BAR = RING + kStages * kStage;
+  static constexpr int kFull = 0;                     // [kStages]
+  static constexpr int kEmpty = kStages;              // [kStages]
+  static constexpr int kDone = 2 * kStages;
+  static constexpr int kDrain = 2 * kStages + 1;
+  static constexpr int kNumBars = 2 * kStages + 2;
+  static constexpr uint32_t MISC = BAR + kNumBars * 8;
+  static constexpr uint32_t kAlloc = MISC + 16 + 1024;
+  static constexpr uint32_t kCols = D;               // fp32 dQ accumulator columns
+};
+constexpr int kDqGemmThreads = 128;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kDqGemmThreads, 1)
+    dq_gemm_kernel(const T* __restrict__ ds, const __grid_constant__ CUtensorMap tmk,
+                   const __grid_constant__ CUtensorMap tmdq, T* __restrict__ dq, float scale,
+                   MaskParams mp, const int32_t* __restrict__ row_ptr,
+                   const int32_t* __restrict__ col_idx, const int32_t* __restrict__ csc_pos,
+                   int nnz, int heads, int kv_group, Strides3 sdq, int* status) {
+  using L = DqGemmLayout<D>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdesc = idesc_f16(kBF16, kT, D, true, true);  // M=128 q, N=D
+  constexpr int kBoxes = D / 64;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sb + L::BAR + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ti = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int hh = bh % heads, bb = bh / heads;
+  const int n_tj = ceil_div_dev(mp.n_kv, kT);
+  const PlanSpan span = plan_span(row_ptr, ti, n_tj, (int64_t)gridDim.x * n_tj, status);
+  const int e0 = span.e0;
+  const int nk = span.n;
+
+  if (nk == 0) {  // the tile's rows see no key: dQ = 0
+    for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
+      const int rr = idx / (D / 8), cc = idx % (D / 8);
+      const int row = ti * kT + rr;
+      if (row < mp.n_q)
+        reinterpret_cast<uint4*>(dq + bb * sdq.b + hh * sdq.h + (int64_t)row * sdq.n)[cc] =
+            make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  const int64_t tile0 = (int64_t)bh * nnz;   // this query (b, h)'s first stored dS tile
+  // (dS_ij^T, K_j) of CSR entry e0 + p into ring stage p % kStages
+  auto load = [&](int p) {
+    const int s = p % L::kStages;
+    const int kt = plan_index(plan_entry(col_idx, e0 + p, n_tj, status));
+    const int cp = bounded(__ldg(csc_pos + e0 + p), nnz, status);
+    const uint32_t dst = sb + L::RING + (uint32_t)s * L::kStage;
+    mbar_expect_tx(bar(L::kFull + s), L::kStage);
+    bulk_load(dst, ds + (size_t)(tile0 + cp) * (kT * kT), L::kDsTile, bar(L::kFull + s));
+    for (int b = 0; b < kBoxes; ++b)
+      tma_load_4d(dst + L::kDsTile + (uint32_t)b * 16384u, &tmk, bar(L::kFull + s), 64 * b,
+                  kt * kT, hh / kv_group, bb);
+  };
+  const int first = min(nk, L::kStages);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(bar(L::kFull + s), 1);
+      mbar_init(bar(L::kEmpty + s), 1);
+    }
+    mbar_init(bar(L::kDone), 1);
+    mbar_init(bar(L::kDrain), 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+    // the first stages are requested before the TMEM allocation and the
+    // CTA-wide sync, so their latency overlaps them
+    for (int p = 0; p < first; ++p) load(p);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool ok = true;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int issued = first;
+    if (lane == 0) {
+      for (int p = first; p < nk; ++p) {
+        const int s = p % L::kStages, f = p / L::kStages;
+        if (!wait_bar(bar(L::kEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status)) break;
+        load(p);
+        issued = p + 1;
+      }
+      // every copy this thread issued lands before the CTA can exit
+      for (int s = 0; s < L::kStages; ++s) {
+        const int fills = issued > s ? (issued - 1 - s) / L::kStages + 1 : 0;
+        if (fills) wait_bar_drain(bar(L::kFull + s), (uint32_t)((fills - 1) & 1), status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    for (int p = 0; p < nk; ++p) {
+      const int s = p % L::kStages;
+      if (!wait_bar_w(bar(L::kFull + s), (uint32_t)((p / L::kStages) & 1), abort_flag, status))
+        break;
+      tc_fence_after();
+      const uint64_t da = desc_mnmajor(sb + L::RING + (uint32_t)s * L::kStage, 16384u);
+      const uint64_t db = desc_mnmajor(sb + L::RING + (uint32_t)s * L::kStage + L::kDsTile, 16384u);
+#pragma unroll
+      for (int kk = 0; kk < kT / 16; ++kk)
+        mma_f16_ss_w(tmem, desc_advance(da, (uint32_t)kk * 2048u),
+                     desc_advance(db, (uint32_t)kk * 2048u), kIdesc, (p > 0 || kk > 0) ? 1u : 0u);
+      tc_commit_w(bar(L::kEmpty + s));
+    }
+    tc_commit_w(bar(L::kDone));
+    tc_commit_w(bar(L::kDrain));
+    wait_bar_drain(bar(L::kDrain), 0, status);
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  // thread r holds query row r of dQ; staged in ring stage 0's dS buffer
+  // (free once every MMA is done) as D/64 swizzled [128][64] boxes
+  ok = wait_bar(bar(L::kDone), 0, abort_flag, status) && !*abort_flag;
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (ok) {
+    tc_fence_after();
+    const int r = threadIdx.x;
+    const uint32_t t_acc = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t t[32];
+      tmem_ld32(t_acc + 32u * c, t);
+      tmem_wait_ld();
+      uint32_t w[16];
+#pragma unroll
+      for (int i2 = 0; i2 < 16; ++i2)
+        w[i2] = pack2<T>(__uint_as_float(t[2 * i2]) * scale, __uint_as_float(t[2 * i2 + 1]) * scale);
+      const uint32_t region = sb + L::RING + (uint32_t)((32 * c) >> 6) * 16384u;
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) {
+        const uint32_t addr = region + sw128_offset((uint32_t)r, (uint32_t)((32 * c) & 63) + 8u * i2);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * i2]),
+                     "r"(w[4 * i2 + 1]), "r"(w[4 * i2 + 2]), "r"(w[4 * i2 + 3])
+                     : "memory");
+      }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1, kDqGemmThreads);
+    if (threadIdx.x == 0) {
+      for (int b = 0; b < kBoxes; ++b)
+        tma_store_4d(&tmdq, sb + L::RING + (uint32_t)b * 16384u, 64 * b, ti * kT, hh, bb);
+      bulk_commit();
+      bulk_wait_read0();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kCols);
+  }
+}
+
 template <typename T, int D>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
                   const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
                   const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri,
-                  float* part_ws, int sink_parts, int* status, cudaStream_t s) {
+                  float* part_ws, int sink_parts, const int32_t* csc_pos, int nnz, void* ds_ws,
+                  int* status, cudaStream_t s) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv;
@@ -905,10 +1145,15 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
   if (int rc = make_tmap_4d(&mdq, dq, kBF16, D, nq, nh, nb, vw.dq, kT)) return rc;
   if (int rc = make_tmap_4d(&mdk, dk, kBF16, D, nkv, nhk, nb, vw.dk, kT)) return rc;
   if (int rc = make_tmap_4d(&mdv, dv, kBF16, D, nkv, nhk, nb, vw.dv, kT)) return rc;
+  // stored dS: BH * nnz tiles of [128 keys][128 queries] 16-bit elements,
+  // each 32 KB kept in the shared-memory layout it is produced and consumed
+  // in (two 128-byte-swizzled [128][64] halves), copied by untiled bulk copies
+  const bool ds = ds_ws != nullptr;
   const float sl = scale * kLog2e;
-  {
-    using L = DkdvLayout<D>;
-    auto kern = dkdv_tc_kernel<T, D>;
+  auto run_dkdv = [&](auto ds_tag) -> int {
+    constexpr bool DS = decltype(ds_tag)::value;
+    using L = DkdvLayout<D, DS>;
+    auto kern = dkdv_tc_kernel<T, D, DS>;
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)L::kAlloc),
                             "cudaFuncSetAttribute(dkdv_tc)"))
@@ -918,10 +1163,16 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     {
       LaunchScope ls("dkdv_tc_kernel", s);
       kern<<<(n_tj - 1 + sink_parts) * units, kBwdThreads, L::kAlloc, s>>>(
-          mq, mk, mv, mdo, mdk, mdv, (T*)dk, (T*)dv, lse, delta, scale, sl, mp, kv_cp, kv_ri,
-          units, n_tj, vw.heads, vw.kv_group, vw.dk, vw.dv, part_ws, sink_parts, status);
+          mq, mk, mv, mdo, mdk, mdv, (T*)ds_ws, nnz, (T*)dk, (T*)dv, lse, delta, scale, sl, mp,
+          kv_cp,
+          kv_ri, units, n_tj, vw.heads, vw.kv_group, vw.dk, vw.dv, part_ws, sink_parts, status);
     }
-    if (int rc = check_launch("dkdv_tc_kernel")) return rc;
+    return check_launch("dkdv_tc_kernel");
+  };
+  {
+    const int n_tj = ceil_div_i(mp.n_kv, kT);
+    const int units = BH / vw.kv_group;  // (batch, key/value head) pairs
+    if (int rc = ds ? run_dkdv(std::true_type{}) : run_dkdv(std::false_type{})) return rc;
     if (sink_parts > 1) {
       LaunchScope ls("dkdv_sink_reduce_kernel", s);
       dkdv_sink_reduce_kernel<T, D><<<units, 256, 0, s>>>(part_ws, (T*)dk, (T*)dv, sink_parts,
@@ -930,6 +1181,21 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     }
   }
   if (int rc = check_launch("dkdv_sink_reduce_kernel")) return rc;
+  if (ds) {
+    using L = DqGemmLayout<D>;
+    auto kern = dq_gemm_kernel<T, D>;
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)L::kAlloc),
+                            "cudaFuncSetAttribute(dq_gemm)"))
+      return rc;
+    dim3 grid(ceil_div_i(mp.n_q, kT), BH);
+    LaunchScope ls("dq_gemm_kernel", s);
+    kern<<<grid, kDqGemmThreads, L::kAlloc, s>>>((const T*)ds_ws, mk, mdq, (T*)dq, scale, mp,
+                                                 dq_rp, dq_ci,
+                                                 csc_pos, nnz, vw.heads, vw.kv_group, vw.dq,
+                                                 status);
+    return check_launch("dq_gemm_kernel");
+  }
   {
     using L = DqLayout<D>;
     auto kern = dq_tc_kernel<T, D>;
@@ -959,11 +1225,20 @@ int64_t tc_bwd_split_bytes(int64_t BH, int kv_group, int64_t D) {
   return BH / kv_group * (int64_t)kv_group * 2 * kT * D * (int64_t)sizeof(float);
 }
 
+// Bytes of the stored dS tiles (16-bit [128 keys][128 queries] per query
+// (b, h) and kept 128 x 128 tile), or 0 where the dS path does not apply
+// (head_dim 64 keeps the recomputing dQ kernel).
+int64_t tc_bwd_ds_bytes(int64_t BH, int64_t nnz, int64_t D) {
+  if (D != 128 || BH <= 0 || nnz <= 0 || BH * nnz >= (1ll << 31)) return 0;
+  return BH * nnz * (int64_t)kT * kT * 2;
+}
+
 int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const void* o,
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta, int BH,
            float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
            const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, void* split_ws,
-           int64_t split_ws_bytes, int* status, cudaStream_t s) {
+           int64_t split_ws_bytes, const int32_t* csc_pos, int64_t nnz, void* ds_ws,
+           int64_t ds_ws_bytes, int* status, cudaStream_t s) {
   if (int rc = generic_delta(dtype, o, dout, delta, BH, mp.n_q, D, vw, s)) return rc;
   const bool bf = dtype == SBFA_BF16;
   // split the sink tile over the group's query heads when the caller gave
@@ -973,9 +1248,15 @@ int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const 
                      ((uintptr_t)split_ws & 15u) == 0;
   float* part = split ? static_cast<float*>(split_ws) : nullptr;
   const int parts = split ? vw.kv_group : 1;
+  // dQ from stored dS when the caller gave room for it
+  const int64_t ds_need = tc_bwd_ds_bytes(BH, nnz, D);
+  const bool use_ds = ds_need > 0 && ds_ws != nullptr && csc_pos != nullptr &&
+                      ds_ws_bytes >= ds_need && ((uintptr_t)ds_ws & 15u) == 0;
+  void* dsw = use_ds ? ds_ws : nullptr;
+  const int nz = use_ds ? (int)nnz : 0;
 #define SBFA_BWD(TT, DD)                                                                        \
   return launch_bwd_tc<TT, DD>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw, dq_rp, \
-                               dq_ci, kv_cp, kv_ri, part, parts, status, s)
+                               dq_ci, kv_cp, kv_ri, part, parts, csc_pos, nz, dsw, status, s)
   if (D == 128) {
     if (bf) SBFA_BWD(__nv_bfloat16, 128);
     SBFA_BWD(__half, 128);

@@ -44,8 +44,10 @@ int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const 
            const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
            int BH, float scale, const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
            const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri, void* split_ws,
-           int64_t split_ws_bytes, int* status, cudaStream_t s);
+           int64_t split_ws_bytes, const int32_t* csc_pos, int64_t nnz, void* ds_ws,
+           int64_t ds_ws_bytes, int* status, cudaStream_t s);
 int64_t tc_bwd_split_bytes(int64_t BH, int kv_group, int64_t D);
+int64_t tc_bwd_ds_bytes(int64_t BH, int64_t nnz, int64_t D);
 namespace tc {
 bool tma_compatible(const void* base, const Strides3& st);
 }
@@ -224,7 +226,7 @@ int check_tma(const void* const* ptrs, const Strides3* const* st, int count, con
 
 using namespace sbfa;
 
-extern "C" int sbfa_abi_version(void) { return 4; }
+extern "C" int sbfa_abi_version(void) { return 5; }
 
 extern "C" int64_t sbfa_launch_count(void) { return g_launches.load(); }
 
@@ -352,7 +354,8 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
                         int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
                         const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
                         const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
-                        void* split_ws, int64_t split_ws_bytes, void* stream) {
+                        void* split_ws, int64_t split_ws_bytes, const int32_t* dq_csc_pos,
+                        int64_t nnz, void* ds_ws, int64_t ds_ws_bytes, void* stream) {
   if (int rc = check_common(B, H, n_q, n_kv, head_dim, dtype, sink, window, block_mask,
                             block_m, block_n))
     return rc;
@@ -371,7 +374,8 @@ extern "C" int sbfa_bwd(const void* q, const void* k, const void* v, const void*
     if (int rc = check_tma(ptrs, st, 7, "sbfa_bwd")) return rc;
     return tc_bwd(dtype, (int)head_dim, q, k, v, o, lse, dout, dq, dk, dv, delta_ws, BH,
                   softmax_scale, mp, vw, dq_row_ptr, dq_col_idx, kv_col_ptr, kv_row_idx,
-                  split_ws, split_ws_bytes, device_status_ptr(), s);
+                  split_ws, split_ws_bytes, dq_csc_pos, nnz, ds_ws, ds_ws_bytes,
+                  device_status_ptr(), s);
   }
   if (!generic_supports(dtype, head_dim))
     return fail(SBFA_ERR_UNSUPPORTED, "head_dim too large (max 256; 128 for float64)");
@@ -411,6 +415,12 @@ extern "C" int64_t sbfa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t head_d
   if (kv_heads <= 0) kv_heads = H;
   if (kv_heads > H || H % kv_heads != 0 || !use_tc(1, dtype, head_dim)) return 0;
   return tc_bwd_split_bytes(B * H, (int)(H / kv_heads), head_dim);
+}
+
+extern "C" int64_t sbfa_bwd_ds_workspace_bytes(int64_t B, int64_t H, int64_t head_dim,
+                                               int dtype, int64_t nnz) {
+  if (B <= 0 || H <= 0 || !use_tc(1, dtype, head_dim)) return 0;
+  return tc_bwd_ds_bytes(B * H, nnz, head_dim);
 }
 
 extern "C" int64_t sbfa_decode_workspace_bytes(int64_t B, int64_t H, int64_t n_kv,

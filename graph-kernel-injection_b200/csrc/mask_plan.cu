@@ -146,6 +146,28 @@ __global__ void plan_scan_kernel(int32_t* row_ptr, int n_rows, int32_t* col_ptr,
   if (threadIdx.x == 0 && nnz != nullptr && (blockIdx.x == 0 || row_ptr == nullptr)) *nnz = carry;
 }
 
+// For every CSR entry (tile row i, tile column j) of a plan, the position of
+// the same tile in the CSC lists: a binary search for i in column j's
+// ascending row list.  One CTA per tile row (grid-strided).
+__global__ void plan_csc_pos_kernel(const int32_t* __restrict__ row_ptr,
+                                    const int32_t* __restrict__ col_idx,
+                                    const int32_t* __restrict__ col_ptr,
+                                    const int32_t* __restrict__ row_idx, int n_ti,
+                                    int32_t* __restrict__ csc_pos) {
+  for (int i = blockIdx.x; i < n_ti; i += gridDim.x) {
+    const int p1 = row_ptr[i + 1];
+    for (int p = row_ptr[i] + threadIdx.x; p < p1; p += blockDim.x) {
+      const int j = plan_index(col_idx[p]);
+      int lo = col_ptr[j], hi = col_ptr[j + 1];
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (plan_index(row_idx[mid]) < i) lo = mid + 1; else hi = mid;
+      }
+      csc_pos[p] = lo;
+    }
+  }
+}
+
 int grid_for(int64_t total) {
   int64_t g = (total + 255) / 256;
   return (int)std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32));
@@ -229,4 +251,19 @@ extern "C" int sbfa_build_plan(const int32_t* block_mask, int64_t n_q, int64_t n
     plan_line_kernel<1><<<lines, 256, 0, s>>>(g, row_ptr, col_idx, col_ptr, row_idx);
   }
   return check_launch("plan_line_kernel<fill>");
+}
+
+extern "C" int sbfa_plan_csc_positions(const int32_t* row_ptr, const int32_t* col_idx,
+                                       const int32_t* col_ptr, const int32_t* row_idx,
+                                       int64_t n_ti, int32_t* csc_pos, void* stream) {
+  if (!row_ptr || !col_idx || !col_ptr || !row_idx || !csc_pos)
+    return fail(SBFA_ERR_INVALID, "sbfa_plan_csc_positions: NULL plan pointer");
+  if (n_ti <= 0 || n_ti >= (1ll << 31)) return fail(SBFA_ERR_INVALID, "n_ti out of range");
+  cudaStream_t s = (cudaStream_t)stream;
+  {
+    LaunchScope ls("plan_csc_pos_kernel", s);
+    plan_csc_pos_kernel<<<(int)std::min<int64_t>(n_ti, 148 * 8), 128, 0, s>>>(
+        row_ptr, col_idx, col_ptr, row_idx, (int)n_ti, csc_pos);
+  }
+  return check_launch("plan_csc_pos_kernel");
 }

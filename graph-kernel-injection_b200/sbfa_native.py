@@ -46,8 +46,10 @@ _SIGNATURES = {
                   _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _i32),
     "sbfa_bwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                   _i64, _i32, _f64, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
-                  _vp, _i64, _vp, _i64, _vp], _i32),
+                  _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp], _i32),
     "sbfa_bwd_workspace_bytes": ([_i64, _i64, _i64, _i32, _i64], _i64),
+    "sbfa_bwd_ds_workspace_bytes": ([_i64, _i64, _i64, _i32, _i64], _i64),
+    "sbfa_plan_csc_positions": ([_vp, _vp, _vp, _vp, _i64, _vp, _vp], _i32),
     "sbfa_decode": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f64, _i32, _i64,
                      _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp], _i32),
     "sbfa_decode_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),

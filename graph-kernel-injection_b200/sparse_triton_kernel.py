@@ -30,6 +30,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 import weakref
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
@@ -187,6 +188,40 @@ def _plan_for(mask: torch.Tensor, pass_id: int, dtype: torch.dtype, head_dim: in
     return _PLANS.get(mask, key, lambda: build_plan(mask, n_q, n_kv, block_m, block_n, tm, tn))
 
 
+def _plan_nnz(plan: dict) -> int:
+    """Kept tiles of a plan on the host (read once per plan)."""
+    if "nnz_host" not in plan:
+        plan["nnz_host"] = int(plan["nnz"].item())
+    return plan["nnz_host"]
+
+
+def _csc_positions(plan: dict, dev: torch.device) -> torch.Tensor:
+    """For every CSR entry of a plan, the CSC position of the same tile
+    (built once per plan): where the dK/dV pass stores that tile's dS."""
+    if "csc_pos" not in plan:
+        pos = torch.empty_like(plan["col_idx"])
+        native.check(native.lib().sbfa_plan_csc_positions(
+            plan["row_ptr"].data_ptr(), plan["col_idx"].data_ptr(), plan["col_ptr"].data_ptr(),
+            plan["row_idx"].data_ptr(), plan["row_ptr"].numel() - 1, pos.data_ptr(),
+            native.stream_ptr(dev)), "plan_csc_positions")
+        plan["csc_pos"] = pos
+    return plan["csc_pos"]
+
+
+DS_BUDGET_ENV = "SBFA_BWD_DS_MAX_BYTES"
+
+
+def _ds_budget(dev: torch.device) -> int:
+    """Most device bytes a backward call may take for stored dS tiles:
+    ``SBFA_BWD_DS_MAX_BYTES`` when set (0 keeps the recomputing dQ kernel),
+    else a quarter of the device's memory, at most half of what is free."""
+    env = os.environ.get(DS_BUDGET_ENV)
+    if env is not None:
+        return int(env)
+    free, total = torch.cuda.mem_get_info(dev)
+    return min(total // 4, free // 2)
+
+
 # ---------------------------------------------------------------------------
 # Autograd bridge
 # ---------------------------------------------------------------------------
@@ -342,6 +377,13 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
         with torch.cuda.device(dev):
             p_dq = _plan_for(block_mask, 1, q.dtype, D, N_Q, N_KV, ctx.block_m, ctx.block_n)
             p_kv = _plan_for(block_mask, 2, q.dtype, D, N_Q, N_KV, ctx.block_m, ctx.block_n)
+            # the dK/dV pass stores dS for a dQ GEMM when the tiles fit the budget
+            ds_ws, ds_bytes, csc = None, 0, None
+            if p_dq is p_kv:
+                need = int(L.sbfa_bwd_ds_workspace_bytes(B, H, D, code, _plan_nnz(p_dq)))
+                if 0 < need <= _ds_budget(dev):
+                    ds_ws = torch.empty(need, dtype=torch.uint8, device=dev)
+                    csc, ds_bytes = _csc_positions(p_dq, dev), need
             native.check(L.sbfa_bwd(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                 do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr(),
@@ -350,7 +392,9 @@ class _BlockSparseFlashAttention(torch.autograd.Function):
                 ctx.block_m, ctx.block_n, p_dq["row_ptr"].data_ptr(),
                 p_dq["col_idx"].data_ptr(), p_kv["col_ptr"].data_ptr(),
                 p_kv["row_idx"].data_ptr(), _stride_array(q, k, v, o, do, dq, dk, dv),
-                kv_heads, native.ptr(split_ws), ws_bytes, native.stream_ptr(dev)), "bwd")
+                kv_heads, native.ptr(split_ws), ws_bytes, native.ptr(csc),
+                _plan_nnz(p_dq) if csc is not None else 0, native.ptr(ds_ws), ds_bytes,
+                native.stream_ptr(dev)), "bwd")
         return dq, dk, dv, None, None, None, None, None, None, None
 
 

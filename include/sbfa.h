@@ -120,6 +120,13 @@ int sbfa_build_plan(const int32_t* block_mask, int64_t n_q, int64_t n_kv,
                     int32_t* row_ptr, int32_t* col_idx, int32_t* col_ptr,
                     int32_t* row_idx, int32_t* nnz_out, void* stream);
 
+/* For every CSR entry p of a plan (both lists built by sbfa_build_plan), the
+ * position in row_idx of the same tile: csc_pos: int32[nnz].  Used by
+ * sbfa_bwd to find the dS tile the dK/dV pass stored for CSR entry p. */
+int sbfa_plan_csc_positions(const int32_t* row_ptr, const int32_t* col_idx,
+                            const int32_t* col_ptr, const int32_t* row_idx, int64_t n_ti,
+                            int32_t* csc_pos, void* stream);
+
 /* Tile sizes (tile_m, tile_n) whose plan the given pass expects.
  * pass: 0 = forward, 1 = backward dQ (CSR), 2 = backward dK/dV (CSC),
  * 3 = decode (n_q == 1). */
@@ -177,7 +184,15 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
  * group; given this scratch, its dK/dV work is split over one CTA per query
  * head and the fp32 partials are summed by a second kernel, instead of one
  * CTA streaming all of them.  NULL (or too small) keeps the single CTA;
- * results agree to rounding. */
+ * results agree to rounding.
+ * ds_ws: optional caller scratch (16-byte aligned) of
+ * sbfa_bwd_ds_workspace_bytes() bytes, with dq_csc_pos from
+ * sbfa_plan_csc_positions() and nnz the plan's kept-tile count (the dQ and
+ * dK/dV plans must then be the same plan).  Given it, the dK/dV pass also
+ * stores every 16-bit dS tile there and dQ becomes a GEMM over the stored
+ * tiles, instead of a third pass that recomputes S, P and dP; NULL keeps that
+ * pass.  The two give the same dQ to rounding (the dS values are the dK/dV
+ * pass's). */
 int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              const float* lse, const void* dout, void* dq, void* dk, void* dv,
              float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
@@ -186,7 +201,17 @@ int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              int64_t block_m, int64_t block_n, const int32_t* dq_row_ptr,
              const int32_t* dq_col_idx, const int32_t* kv_col_ptr,
              const int32_t* kv_row_idx, const int64_t* strides, int64_t kv_heads,
-             void* split_ws, int64_t split_ws_bytes, void* stream);
+             void* split_ws, int64_t split_ws_bytes, const int32_t* dq_csc_pos,
+             int64_t nnz, void* ds_ws, int64_t ds_ws_bytes, void* stream);
+
+/* Bytes of the stored dS tiles sbfa_bwd can use for this shape: B * H * nnz
+ * tiles of 128 x 128 16-bit elements (nnz = kept 128 x 128 tiles of the
+ * plan), or 0 where that path does not apply (dtype / head_dim other than
+ * fp16 / bf16 with head_dim 128, or B * H * nnz >= 2^31).  No upstream
+ * counterpart (upstream recomputes dS in its dQ kernel,
+ * sparse_triton_kernel.py:512-601). */
+int64_t sbfa_bwd_ds_workspace_bytes(int64_t B, int64_t H, int64_t head_dim, int dtype,
+                                    int64_t nnz);
 
 /* Scratch bytes of the split first key tile in sbfa_bwd (0 when nothing is
  * split: no grouping, or a dtype / head_dim the tensor-core kernels do not

@@ -86,14 +86,23 @@ def test_golden_cases(golden, name, dtype):
     close(dv, refs["dv"], dtype, "bwd")
 
 
+@pytest.mark.parametrize("dq_path", ["stored", "recompute"])
 @pytest.mark.parametrize("name", [c[0] for c in ATTN_TC_CASES])
-def test_tensor_core_golden_cases(golden_dir, name):
+def test_tensor_core_golden_cases(golden_dir, monkeypatch, name, dq_path):
     """Upstream outputs at the tensor-core shapes (16-bit inputs, head_dim
     128 / 64, 128 x 128 blocks), produced by the reference itself: the
-    tcgen05 forward, dK/dV and dQ kernels against them directly."""
+    tcgen05 forward, dK/dV and both dQ kernels (the GEMM over stored dS at
+    head_dim 128, the recomputing pass) against them directly."""
     from tests.test_oracle_golden import tc_case_inputs
     g = np.load(os.path.join(golden_dir, "attention_tc_cases.npz"))
     (B, H, n_q, n_kv, D, bm, bn, causal, s, w), dt, mask, ins, outs = tc_case_inputs(g, name)
+    if dq_path == "stored" and D != 128:
+        pytest.skip("dS is stored for the dQ GEMM at head_dim 128 only")
+    if dq_path == "recompute":
+        monkeypatch.setenv(stk.DS_BUDGET_ENV, "0")
+    else:
+        monkeypatch.delenv(stk.DS_BUDGET_ENV, raising=False)
+    want_dq = "dq_gemm_kernel" if dq_path == "stored" else "dq_tc_kernel"
     qd, kd, vd, dod = (ins[x].to(DEV) for x in ("q", "k", "v", "do"))
     native.timing_read()
     native.timing(True)
@@ -103,7 +112,7 @@ def test_tensor_core_golden_cases(golden_dir, name):
         ran = native.timing_read()
     finally:
         native.timing(False)
-    assert {"fwd_tc_kernel", "dkdv_tc_kernel", "dq_tc_kernel"} <= set(ran), ran
+    assert {"fwd_tc_kernel", "dkdv_tc_kernel", want_dq} <= set(ran), ran
     for nm, got in (("O", o), ("dQ", dq), ("dK", dk), ("dV", dv)):
         check_half(got, outs[nm.lower()], dt, f"{name} {nm}")
     assert native.device_status() == 0
@@ -361,6 +370,53 @@ def test_grouped_query_decode_custom_mask_and_grad(dtype, D, H, Hkv, bn):
     # no kept block: every head's output is 0 (upstream's empty-row rule)
     o, *_ = run(q, k, v, torch.zeros_like(mask), 1, bn, False, S, W)
     assert torch.equal(o, torch.zeros_like(o))
+    assert native.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype,H,Hkv", [(torch.bfloat16, 2, 2), (torch.float16, 4, 1)])
+def test_stored_ds_dq_matches_recompute(monkeypatch, dtype, H, Hkv):
+    """At head_dim 128 the dK/dV pass stores dS and dQ is a GEMM over the
+    stored tiles (dq_gemm_kernel); with a zero budget the third pass
+    recomputes S, P and dP instead (dq_tc_kernel).  Both match the oracle,
+    dK and dV are bit-identical between them (same pass, same arithmetic),
+    and dQ agrees to rounding."""
+    B, N, S, W, D = 1, 700, 4, 256, 128
+    gen = torch.Generator(device=DEV).manual_seed(17)
+    q = torch.randn(B, H, N, D, generator=gen, device=DEV, dtype=dtype)
+    k = torch.randn(B, Hkv, N, D, generator=gen, device=DEV, dtype=dtype)
+    v = torch.randn(B, Hkv, N, D, generator=gen, device=DEV, dtype=dtype)
+    do = torch.randn(B, H, N, D, generator=gen, device=DEV, dtype=dtype)
+    mask = stk.make_streaming_mask(N, N, stk.StreamingMaskSpec(S, W), 128, 128, DEV)
+    outs = {}
+    for name, budget in (("stored", None), ("recompute", "0")):
+        if budget is None:
+            monkeypatch.delenv(stk.DS_BUDGET_ENV, raising=False)
+        else:
+            monkeypatch.setenv(stk.DS_BUDGET_ENV, budget)
+        native.timing_read()
+        native.timing(True)
+        try:
+            outs[name] = run(q, k, v, mask, 128, 128, True, S, W, do=do)
+            ran = native.timing_read()
+        finally:
+            native.timing(False)
+        want, other = ("dq_gemm_kernel", "dq_tc_kernel") if budget is None else (
+            "dq_tc_kernel", "dq_gemm_kernel")
+        assert want in ran and other not in ran, ran
+    rep = H // Hkv
+    ke, ve = (t.repeat_interleave(rep, dim=1) for t in (k, v))
+    ro, rdq, rdk, rdv = orc.attention_forward_backward(
+        q.double().cpu(), ke.double().cpu(), ve.double().cpu(), do.double().cpu(), mask.cpu(),
+        block_m=128, block_n=128, is_causal=True, sink_size=S, window_size=W)
+    rdk = rdk.view(B, Hkv, rep, N, D).sum(2)
+    rdv = rdv.view(B, Hkv, rep, N, D).sum(2)
+    for name, (o, dq, dk, dv) in outs.items():
+        check_half(dq, rdq, dtype, f"{name} dQ")
+        check_half(dk, rdk, dtype, f"{name} dK")
+        check_half(dv, rdv, dtype, f"{name} dV")
+    a, b = outs["stored"], outs["recompute"]
+    assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+    assert (a[1].float() - b[1].float()).abs().max().item() < 2e-2
     assert native.device_status() == 0
 
 

@@ -70,13 +70,24 @@ def _fwd_bwd(h, q, k, v, do, mask, bm, bn, causal, s, w):
     delta = torch.empty(B, H, n_q, dtype=torch.float32, device=DEV)
     ws_bytes = int(h.sbfa_bwd_workspace_bytes(B, H, D, code, hk))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=DEV)
+    # stored-dS path (dQ as a GEMM over the dK/dV pass's dS tiles) where it applies
+    nnz = stk._plan_nnz(p1)
+    ds_bytes = int(h.sbfa_bwd_ds_workspace_bytes(B, H, D, code, nnz)) if p1 is p2 else 0
+    ds = torch.empty(max(ds_bytes, 16), dtype=torch.uint8, device=DEV)
+    csc = torch.empty_like(p1["col_idx"])
+    if ds_bytes:
+        assert h.sbfa_plan_csc_positions(p1["row_ptr"].data_ptr(), p1["col_idx"].data_ptr(),
+                                         p1["col_ptr"].data_ptr(), p1["row_idx"].data_ptr(),
+                                         p1["row_ptr"].numel() - 1, csc.data_ptr(), st) == 0
     assert h.sbfa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                       do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                       delta.data_ptr(), B, H, n_q, n_kv, D, code, scale, int(causal), s, w,
                       mask.data_ptr(), bm, bn, p1["row_ptr"].data_ptr(),
                       p1["col_idx"].data_ptr(), p2["col_ptr"].data_ptr(),
                       p2["row_idx"].data_ptr(), _strides(q, k, v, o, do, dq, dk, dv), hk,
-                      ws.data_ptr() if ws_bytes else None, ws_bytes, st) == 0
+                      ws.data_ptr() if ws_bytes else None, ws_bytes,
+                      csc.data_ptr() if ds_bytes else None, nnz if ds_bytes else 0,
+                      ds.data_ptr() if ds_bytes else None, ds_bytes, st) == 0
     torch.cuda.synchronize()
     return o, lse, dq, dk, dv
 

@@ -44,7 +44,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.sbfa_abi_version() == 4
+    assert lib.sbfa_abi_version() == 5
 
 
 def test_validation_errors_without_gpu(lib):
@@ -90,6 +90,19 @@ def test_bwd_workspace_bytes(lib):
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F16, 1) == 8 * 2 * 128 * 64 * 4
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 64, native.F32, 1) == 0
     assert lib.sbfa_bwd_workspace_bytes(1, 8, 128, native.BF16, 3) == 0   # 8 % 3 != 0
+
+
+def test_bwd_ds_workspace_bytes(lib):
+    """Stored-dS scratch: B * H * nnz tiles of 128 x 128 16-bit values for
+    fp16/bf16 at head_dim 128; 0 elsewhere and when the tile count reaches
+    2^31 (TMA coordinates are 32-bit)."""
+    assert lib.sbfa_bwd_ds_workspace_bytes(4, 32, 128, native.BF16, 2151) == \
+        4 * 32 * 2151 * 128 * 128 * 2
+    assert lib.sbfa_bwd_ds_workspace_bytes(1, 2, 128, native.F16, 7) == 2 * 7 * 128 * 128 * 2
+    assert lib.sbfa_bwd_ds_workspace_bytes(4, 32, 64, native.BF16, 2151) == 0
+    assert lib.sbfa_bwd_ds_workspace_bytes(4, 32, 128, native.F32, 2151) == 0
+    assert lib.sbfa_bwd_ds_workspace_bytes(4, 32, 128, native.BF16, 0) == 0
+    assert lib.sbfa_bwd_ds_workspace_bytes(1 << 12, 1 << 10, 128, native.BF16, 1 << 9) == 0
 
 
 def test_debug_library_exports_the_same_symbols():
