@@ -50,6 +50,20 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
   return 64u * (uint32_t)(kk >> 2) + 8u * (uint32_t)(kk & 3);
 }
 
+// Stored dS tiles (dkdv_tc_kernel<..., DS = true> -> dq_gemm_kernel): the
+// 128 x 128 16-bit tile is the A operand (M = 128 queries, K = 128 keys,
+// M-major) of a tcgen05 MMA without swizzle, made of 8 x 8 core matrices of
+// 128 contiguous bytes, each 8 keys x 8 consecutive queries (16 B per key).
+// Core matrices follow each other along the keys (128 B apart), and each
+// group of 8 queries is a 2048-byte plane: element (query q, key k) sits at
+//   (q / 8) * 2048 + k * 16 + (q % 8) * 2  bytes.
+// A thread holding one key's 8 consecutive queries writes one 16-byte piece,
+// and the 32 keys of a warp write 512 contiguous bytes.
+constexpr uint32_t kDsChunkBytes = 2048;  // one plane of 8 queries x 128 keys
+__host__ __device__ constexpr uint32_t ds_tile_offset(int q, int k) {
+  return (uint32_t)(q >> 3) * kDsChunkBytes + (uint32_t)k * 16u + (uint32_t)(q & 7) * 2u;
+}
+
 // ---------------------------------------------------------------------------
 // dK / dV
 // ---------------------------------------------------------------------------
@@ -68,23 +82,23 @@ __device__ __forceinline__ uint32_t a_col128(int kk) {
 // 2i+1 = dO_i.  dS is computed without the softmax scale, which multiplies
 // dK once in the epilogue.
 //
-// With DS the kernel also stores every dS_i^T tile (128 keys x 128 queries,
-// 16-bit) to global memory for dq_gemm_kernel: each compute thread writes its
-// key's 64 columns into a swizzled shared-memory staging tile and warp 3
-// writes the tile out with two TMA stores, at the CSC position of the
-// (query head, key tile, query tile) triple.
+// With DS the kernel also stores every dS_i tile (128 queries x 128 keys,
+// 16-bit) to global memory for dq_gemm_kernel, at the CSC position of the
+// (query head, key tile, query tile) triple, in the layout of a tcgen05
+// operand without swizzle (see ds_tile_offset): each compute thread stores
+// its key's 64 columns straight from registers as eight 16-byte pieces, and
+// every warp-wide store covers 512 contiguous bytes.  Nothing is staged in
+// shared memory, whose bandwidth the MMAs already use in full.
 template <int D, bool DS = false>
 struct DkdvLayout {
   // K, V and a 5-entry ring of 128-column tiles fill 224 KB; 64-column
-  // tiles leave room for 6 ring entries.  With DS the 32 KB dS staging tile
-  // takes one 128-column ring entry.
-  static constexpr int kRing = D > 64 ? (DS ? 4 : 5) : 6;
+  // tiles leave room for 6 ring entries.
+  static constexpr int kRing = D > 64 ? 5 : 6;
   static constexpr uint32_t kTile = kT * D * 2;
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + kTile;
   static constexpr uint32_t RING = V + kTile;               // kRing streamed tiles
-  static constexpr uint32_t DSB = RING + kRing * kTile;      // dS^T staging (DS only)
-  static constexpr uint32_t LS = DSB + (DS ? 2u * 16384u : 0u);  // 2 x 128 floats (LSE * log2 e)
+  static constexpr uint32_t LS = RING + kRing * kTile;       // 2 x 128 floats (LSE * log2 e)
   static constexpr uint32_t DL = LS + 2 * kT * 4;            // 2 x 128 floats (Delta)
   static constexpr uint32_t BAR = DL + 2 * kT * 4;
   static constexpr int kKVFull = 0;
@@ -98,9 +112,7 @@ struct DkdvLayout {
   static constexpr int kDSReady = 8 + 2 * kRing;     // P_i and dS_i packed in TMEM
   static constexpr int kDone = 9 + 2 * kRing;
   static constexpr int kDrain = 10 + 2 * kRing;
-  static constexpr int kStageFull = 11 + 2 * kRing;  // dS_i staged (DS)
-  static constexpr int kStageFree = 12 + 2 * kRing;  // staging read by the TMA store (DS)
-  static constexpr int kNumBars = 13 + 2 * kRing;
+  static constexpr int kNumBars = 11 + 2 * kRing;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kBytes = MISC + 16;
   // D = 128 leaves no room to align the window by hand: the kernel checks
@@ -215,10 +227,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(L::kDSReady), 256);
     mbar_init(bar(L::kDone), 1);
     mbar_init(bar(L::kDrain), 1);
-    if (DS) {
-      mbar_init(bar(L::kStageFull), 256);
-      mbar_init(bar(L::kStageFree), 1);
-    }
     *abort_flag = 0;
     mbar_init_fence();
     // the resident K, V tiles are requested before the TMEM allocation and
@@ -313,22 +321,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::kLFull + slot));
       }
-    } else if (DS && warp == 3) {
-      // ------------------------------------------------------ dS^T store
-      // tile i of this CTA: query head hh * kv_group + head_lo + i / nq, CSC
-      // entry e0 + i % nq; stored as tile (query (b, h)) * nnz + entry
-      for (int i = 0; i < ntot; ++i) {
-        if (!wait_bar_w(bar(L::kStageFull), (uint32_t)(i & 1), abort_flag, status)) break;
-        if (lane == 0) {
-          const int hq = hh * kv_group + head_lo + i / nq;
-          const int tile = (bb * heads + hq) * nnz + e0 + i % nq;
-          bulk_store(ds + (size_t)tile * (kT * kT), sb + L::DSB, 2u * 16384u);
-          bulk_commit();
-          bulk_wait_read0();
-          mbar_arrive(bar(L::kStageFree));
-        }
-        __syncwarp();
-      }
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
       const uint64_t d_k = desc_kmajor(sb + L::K), d_v = desc_kmajor(sb + L::V);
@@ -407,6 +399,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     int32_t ent_next = plan_entry(row_idx, e0, n_ti, status);
     int pos_next = nq > 1 ? 1 : 0;  // (i + 1) % nq, kept as a counter (no division)
+    int pos_i = 0, head_i = 0;      // i % nq and i / nq
     for (int i = 0; i < ntot; ++i) {
       const int slot = i & 1;
       const uint32_t ph = (uint32_t)(i & 1);
@@ -490,23 +483,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(bar(L::kDSReady));
       if constexpr (DS) {
-        // this key's row of dS_i^T, query columns [64g, 64g+64), into the
-        // staging tile once the store of dS_{i-1} has read it
-        if (i > 0 &&
-            !wait_bar_w(bar(L::kStageFree), (uint32_t)((i - 1) & 1), abort_flag, status)) {
-          ok = false;
-          break;
-        }
-        const uint32_t region = sb + L::DSB + (uint32_t)grp * 16384u;
+        // this key's 64 columns of dS_i, straight from registers (tile
+        // (query (b, h)) * nnz + CSC position; see ds_tile_offset)
+        T* dst = ds + (size_t)((bb * heads + hh * kv_group + head_lo + head_i) * nnz + e0 + pos_i) *
+                          (kT * kT) +
+                 ds_tile_offset(64 * grp, r) / sizeof(T);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t addr = region + sw128_offset((uint32_t)r, 8u * c);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(dsk[4 * c]),
-                       "r"(dsk[4 * c + 1]), "r"(dsk[4 * c + 2]), "r"(dsk[4 * c + 3])
-                       : "memory");
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(bar(L::kStageFull));
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(dst + c * (kDsChunkBytes / sizeof(T))) =
+              make_uint4(dsk[4 * c], dsk[4 * c + 1], dsk[4 * c + 2], dsk[4 * c + 3]);
+      }
+      if (++pos_i == nq) {
+        pos_i = 0;
+        ++head_i;
       }
     }
     // epilogue: group 0 writes dV (staged in K's buffer), group 1 writes
@@ -941,18 +930,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // dQ from stored dS (after dkdv_tc_kernel<..., DS = true>)
 // ---------------------------------------------------------------------------
 // dQ_i = scale * sum_j dS_ij K_j over the key tiles j query tile i sees (CSR
-// plan), with dS_ij^T read from the tile dkdv_tc_kernel stored at
+// plan), with dS_ij read from the tile dkdv_tc_kernel stored at
 // (query (b, h)) * nnz + csc_pos[p] for CSR entry p.  One CTA per (query
-// tile, query (b, h)): warp 0 streams (dS_ij^T, K_j) pairs through a ring
-// with TMA, warp 1 issues 128 x D x 128 MMAs (A = dS_ij, M-major from the
-// stored [key][query] tile; B = K_j, N-major) into a TMEM accumulator, and
-// the four warps write dQ (one query row per thread) through a TMA store.
+// tile, query (b, h)): warp 0 streams (dS_ij, K_j) pairs through a ring
+// (dS by one 32 KB bulk copy, byte for byte in its stored layout; K_j by
+// TMA), warp 1 issues 128 x D x 128 MMAs (A = dS_ij, M-major without
+// swizzle; B = K_j, N-major) into a TMEM accumulator, and the four warps
+// write dQ (one query row per thread) through a TMA store.
 // No exponentials, no recomputed S or dP: the kernel moves 32 KB of dS per
 // kept tile and is bound by HBM.
 template <int D>
 struct DqGemmLayout {
   static constexpr int kStages = D > 64 ? 3 : 4;
-  static constexpr uint32_t kDsTile = kT * kT * 2;   // dS^T [128 keys][128 queries]
+  static constexpr uint32_t kDsTile = kT * kT * 2;   // dS [128 queries x 128 keys], ds_tile_offset
   static constexpr uint32_t kKTile = kT * D * 2;     // K_j [128 keys][D]
   static constexpr uint32_t kStage = kDsTile + kKTile;
   static constexpr uint32_t RING = 0;
@@ -1069,11 +1059,14 @@ __global__ void __launch_bounds__(kDqGemmThreads, 1)
       if (!wait_bar_w(bar(L::kFull + s), (uint32_t)((p / L::kStages) & 1), abort_flag, status))
         break;
       tc_fence_after();
-      const uint64_t da = desc_mnmajor(sb + L::RING + (uint32_t)s * L::kStage, 16384u);
+      // A: 16 keys per k-step = ds_tile_offset(0, 16 kk); core matrices 128 B
+      // apart along the keys, 2048 B apart along the queries
+      const uint64_t da =
+          smem_desc_noswizzle(sb + L::RING + (uint32_t)s * L::kStage, 128u, kDsChunkBytes);
       const uint64_t db = desc_mnmajor(sb + L::RING + (uint32_t)s * L::kStage + L::kDsTile, 16384u);
 #pragma unroll
       for (int kk = 0; kk < kT / 16; ++kk)
-        mma_f16_ss_w(tmem, desc_advance(da, (uint32_t)kk * 2048u),
+        mma_f16_ss_w(tmem, desc_advance(da, ds_tile_offset(0, 16 * kk)),
                      desc_advance(db, (uint32_t)kk * 2048u), kIdesc, (p > 0 || kk > 0) ? 1u : 0u);
       tc_commit_w(bar(L::kEmpty + s));
     }

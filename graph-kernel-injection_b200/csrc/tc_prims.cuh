@@ -281,6 +281,20 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_
 __device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t off_bytes) {
   return desc + (uint64_t)(off_bytes >> 4);
 }
+// Shared-memory matrix descriptor without swizzle: the operand is made of
+// core matrices of 8 rows x 16 bytes, each 128 contiguous bytes.  For an
+// MN-major operand a core-matrix row is 8 consecutive M/N elements of one k;
+//    LBO = byte distance between core matrices adjacent along K,
+//    SBO = byte distance between core matrices adjacent along M/N.
+__device__ __forceinline__ uint64_t smem_desc_noswizzle(uint32_t addr, uint32_t lbo_bytes,
+                                                        uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm100; layout type 0: no swizzle
+  return d;
+}
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
   return smem_desc_sw128(addr, 16, 1024);
 }
