@@ -103,7 +103,7 @@ class Dist:
 
 
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
@@ -113,44 +113,67 @@ class ClockSampler:
         self.path = os.path.join("/tmp", f"sbfa_clocks_{os.getpid()}.csv")
 
     def start(self):
+        """Starts sampling every 50 ms and returns once the first sample is
+        written, so that nvidia-smi's own start-up (seconds of host CPU and
+        driver calls) is over before a timed region begins."""
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                 stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and self.proc.poll() is None:
+            self.fh.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
 
-    def stop(self):
+    def stop(self, window=None):
+        """Median SM clock, its maximum and the throttle reasons seen.  With
+        `window` = (t0, t1) in host wall-clock seconds (the timed region),
+        only the samples taken inside it count (the whole run when none
+        fell inside, which `in_window` = false then says)."""
         if self.proc is None:
             return None
+        return self._summary(window)
+
+    def _summary(self, window):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
-        sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in open(self.path):
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 6:
+            if len(parts) < 7:
                 continue
             try:
-                sm.append(float(parts[0]))
-                mx = max(mx, float(parts[1]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[1]), float(parts[2]),
+                             {nm for nm, val in zip(names, parts[3:7]) if val.lower() == "active"}))
             except ValueError:
                 continue
-            for nm, val in zip(names, parts[2:6]):
-                if val.lower() == "active":
-                    reasons.add(nm)
         os.unlink(self.path)
-        if not sm:
+        if not rows:
             return None
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = rows
+        if window is not None:
+            inside = [r for r in rows if window[0] <= r[0] <= window[1]]
+        in_window = window is not None and bool(inside)
+        if not inside:
+            inside = rows
+        sm = sorted(r[1] for r in inside)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": sorted(set().union(*(r[3] for r in inside))),
+                "samples": len(sm), "in_window": in_window,
+                "sm_mhz_min": sm[0]}
 
 
 # ---------------------------------------------------------------------------
@@ -194,7 +217,23 @@ def kernel_kind(name: str):
     return None
 
 
+STEP_MS = []  # device time of each timed step of the last time_steps call (rank-local)
+HOST_MS = []  # host time each of those steps took to enqueue (rank-local)
+WINDOW = None  # host wall-clock (start, end) of that timed region
+
+
 def time_steps(dist, step, steps: int, warmup: int):
+    """Untimed warm-up, then `steps` steps bracketed by a barrier and a
+    device synchronisation on both sides, timed with CUDA events on the
+    launching stream; returns (max-over-ranks ms, our kernel launches,
+    per-kernel device time).  An event after every step also records each
+    step's own device time in STEP_MS, which shows whether a slow run had
+    one stalled step or was slow throughout, and HOST_MS holds the host time
+    each step took to enqueue (a device step much longer than its kernels
+    with a long host step means the GPU waited for the host).  The garbage
+    collector is paused over the timed steps."""
+    global STEP_MS, HOST_MS, WINDOW
+    import gc
     import sbfa_native as native
     for _ in range(warmup):
         step()
@@ -206,17 +245,85 @@ def time_steps(dist, step, steps: int, warmup: int):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     dist.barrier()
-    start.record()
-    for _ in range(steps):
-        step()
-    end.record()
-    torch.cuda.synchronize()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    host = [0.0] * (steps + 1)
+    gc.collect()
+    gc.disable()
+    try:
+        wall0 = time.time()
+        start.record()
+        host[0] = time.perf_counter()
+        for i in range(steps):
+            step()
+            marks[i].record()
+            host[i + 1] = time.perf_counter()
+        end.record()
+        torch.cuda.synchronize()
+    finally:
+        gc.enable()
     dist.barrier()
     native.timing(False)
+    HOST_MS = [(host[i + 1] - host[i]) * 1e3 for i in range(steps)]
+    WINDOW = (wall0, time.time())
+    STEP_MS = [(start if i == 0 else marks[i - 1]).elapsed_time(marks[i]) for i in range(steps)]
     launches = native.launch_count() - n0
     ms = start.elapsed_time(end)
     per_kernel = native.timing_read()
     return dist.max(ms), launches, per_kernel
+
+
+def graph_steps(dist, step, steps: int, warmup: int):
+    """The step captured once into a CUDA graph, then `warmup` untimed and
+    `steps` timed replays, bracketed like time_steps (barrier and device
+    synchronisation on both sides, CUDA events on the launching stream, the
+    max over ranks).  A replay is one host call, so the whole timed region is
+    queued in about a millisecond and a stalled host thread (seen on these
+    shared boxes for tens of ms at a time) cannot leave the GPU idle.  Returns
+    None and the reason when the capture fails."""
+    import sbfa_native as native
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = native.launch_count()
+    try:
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            step()
+    except Exception as exc:  # noqa: BLE001 - reported, the eager timing stands
+        torch.cuda.synchronize()
+        return None, f"capture failed: {str(exc).splitlines()[0][:160]}"
+    per_step = native.launch_count() - n0
+    for _ in range(max(warmup, 1)):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    host = [0.0] * (steps + 1)
+    wall0 = time.time()
+    start.record()
+    host[0] = time.perf_counter()
+    for i in range(steps):
+        graph.replay()
+        marks[i].record()
+        host[i + 1] = time.perf_counter()
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    wall1 = time.time()
+    ms = start.elapsed_time(end)
+    res = {"ms": dist.max(ms), "launches": per_step * steps, "window": (wall0, wall1),
+           "step_ms": [(start if i == 0 else marks[i - 1]).elapsed_time(marks[i])
+                       for i in range(steps)],
+           "host_ms": [(host[i + 1] - host[i]) * 1e3 for i in range(steps)]}
+    del graph
+    torch.cuda.synchronize()
+    return res, "ok"
 
 
 def tensor_peak(pk, clocks):
@@ -416,10 +523,25 @@ def bench_fwdbwd(dist, args, pk, src):
         o.backward(do)
         return o
 
+    # headline: the step replayed from a CUDA graph; per-kernel device
+    # times (the roofline) from an eager timed pass of the same step
     clocks = ClockSampler(dist.local)
     clocks.start()
-    ms, launches, per_kernel = time_steps(dist, step, args.steps, args.warmup)
-    clk = clocks.stop()
+    gres, gwhy = graph_steps(dist, step, args.steps, args.warmup)
+    clk = clocks.stop(gres["window"] if gres is not None else None)
+    eclocks = ClockSampler(dist.local)
+    eclocks.start()
+    e_ms, e_launches, per_kernel = time_steps(dist, step, args.steps, args.warmup)
+    eclk = eclocks.stop(WINDOW)
+    eager = {"ms_per_step": round(e_ms / args.steps, 3), "launches": e_launches,
+             "step_ms_rank0": [round(x, 3) for x in STEP_MS],
+             "host_enqueue_ms_rank0": [round(x, 3) for x in HOST_MS], "clocks": eclk}
+    if gres is None:
+        ms, launches, clk = e_ms, e_launches, eclk
+        step_ms, host_ms = list(STEP_MS), list(HOST_MS)
+    else:
+        ms, launches = gres["ms"], gres["launches"]
+        step_ms, host_ms = gres["step_ms"], gres["host_ms"]
     value = 3.5 * F * args.steps / (ms / 1e3) / 1e12
 
     # verification (outside the timed region)
@@ -470,7 +592,10 @@ def bench_fwdbwd(dist, args, pk, src):
     rl = roofline(per_kernel, F_local, pk, src, clocks=clk, workload="cfg2",
                   scale_units=(stop - start) / units)
     res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
-               nnz=nnz, flops_fwd=F, verify=verify, per_kernel=per_kernel,
+               nnz=nnz, flops_fwd=F, verify=verify, per_kernel=per_kernel, step_ms=step_ms,
+               host_ms=host_ms, eager=eager,
+               timing=("CUDA-graph replays of the captured fwd+bwd step" if gres is not None
+                       else f"eager steps ({gwhy})"),
                units=(start, stop, units))
     del q, k, v, do
     torch.cuda.empty_cache()
@@ -568,7 +693,7 @@ def bench_fwd(dist, args, pk, src):
     clocks = ClockSampler(dist.local)
     clocks.start()
     ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
-    clk = clocks.stop()
+    clk = clocks.stop(WINDOW)
     value = F * steps / (ms / 1e3) / 1e12
     share = (stop - start) / units
     rl = roofline(per_kernel, F * share, pk, src, clocks=clk, workload="cfg3", scale_units=share)
@@ -841,11 +966,17 @@ def main():
         line.update({"value": round(r["value"], 3), "ms_per_step": round(r["ms"] / args.steps, 3),
                      "e2e": r["e2e"], "roofline": r["roofline"], "clocks": r["clocks"],
                      "gpu_launches": r["launches"]})
+        line["config"]["timing"] = (r["timing"] + "; roofline and per-kernel times from an "
+                                    "eager timed pass of the same step")
         start, stop, units = r["units"]
         extra["fwdbwd"] = {"kept_blocks": r["nnz"], "flops_fwd": r["flops_fwd"],
                            "units_rank0": [start, stop], "units_total": units,
                            "verify_rank0": r["verify"],
-                           "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()}}
+                           "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()},
+                           "step_ms_rank0": [round(x, 3) for x in r["step_ms"]],
+                           "host_enqueue_ms_rank0": [round(x, 3) for x in r["host_ms"]],
+                           "timed_as": r["timing"],
+                           "eager_pass": r["eager"]}
         _, mask = kept_blocks(CFG2)
         ex = executed_mma_flops(mask, CFG2, stop - start,
                                 dq_gemms=1 if "dq_gemm_kernel" in r["per_kernel"] else 3)
