@@ -1138,9 +1138,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
   if (int rc = make_tmap_4d(&mdq, dq, kBF16, D, nq, nh, nb, vw.dq, kT)) return rc;
   if (int rc = make_tmap_4d(&mdk, dk, kBF16, D, nkv, nhk, nb, vw.dk, kT)) return rc;
   if (int rc = make_tmap_4d(&mdv, dv, kBF16, D, nkv, nhk, nb, vw.dv, kT)) return rc;
-  // stored dS: BH * nnz tiles of [128 keys][128 queries] 16-bit elements,
-  // each 32 KB kept in the shared-memory layout it is produced and consumed
-  // in (two 128-byte-swizzled [128][64] halves), copied by untiled bulk copies
+  // stored dS: BH * nnz tiles of 128 queries x 128 keys, 16-bit, 32 KB each
+  // in the layout of ds_tile_offset
   const bool ds = ds_ws != nullptr;
   const float sl = scale * kLog2e;
   auto run_dkdv = [&](auto ds_tag) -> int {
