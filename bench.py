@@ -15,10 +15,14 @@ prefill forward (TFLOP/s), config 4 decode (KV GB/s over the 2.1517e9
 visible K/V bytes per step), both split the same way, and config 5 (the FX
 pass on an 8-layer Llama-style decoder, one GPU).
 
+The K timed fwd+bwd steps are replays of the step captured once into a
+CUDA graph (the same kernels; the host queues the whole timed region at
+once, so a stalled host thread cannot idle the GPU); an eager timed pass of
+the same step follows and is reported in ``extra.fwdbwd.eager_pass``.
 ``e2e`` runs the same step through the public API from pinned host buffers
 (Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step).
-``roofline`` uses the dominant kernel's duration measured inside the timed
-region with CUDA events recorded by libsbfa around each launch.
+``roofline`` uses the dominant kernel's duration measured in the eager timed
+pass with CUDA events recorded by libsbfa around each launch.
 ``--impl reference`` times the upstream eager masked-attention algorithm
 (the CPU oracle port) on the host cores instead.
 """
