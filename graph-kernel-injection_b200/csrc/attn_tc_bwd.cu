@@ -25,11 +25,15 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "tc_attn_common.cuh"
 
 namespace sbfa {
+
+int device_sm_count();
+
 namespace {
 
 using namespace tc;
@@ -931,14 +935,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------------------------
 // dQ_i = scale * sum_j dS_ij K_j over the key tiles j query tile i sees (CSR
 // plan), with dS_ij read from the tile dkdv_tc_kernel stored at
-// (query (b, h)) * nnz + csc_pos[p] for CSR entry p.  One CTA per (query
-// tile, query (b, h)): warp 0 streams (dS_ij, K_j) pairs through a ring
-// (dS by one 32 KB bulk copy, byte for byte in its stored layout; K_j by
-// TMA), warp 1 issues 128 x D x 128 MMAs (A = dS_ij, M-major without
-// swizzle; B = K_j, N-major) into a TMEM accumulator, and the four warps
-// write dQ (one query row per thread) through a TMA store.
-// No exponentials, no recomputed S or dP: the kernel moves 32 KB of dS per
-// kept tile and is bound by HBM.
+// (query (b, h)) * nnz + csc_pos[p] for CSR entry p.  No exponentials, no
+// recomputed S or dP: the kernel moves 32 KB of dS per kept tile and is
+// bound by HBM.  Persistent: one CTA per SM walks the (query tile,
+// query (b, h)) items head-major, so its load pipeline never drains between
+// items:
+//   warp 0      streams (dS_ij, K_j) pairs of item after item through a
+//               ring (dS by one 32 KB bulk copy, byte for byte in its stored
+//               layout; K_j by TMA);
+//   warp 1      issues the 128 x D x 128 MMAs (A = dS_ij, M-major without
+//               swizzle; B = K_j, N-major) into one of two TMEM
+//               accumulators, alternating per item;
+//   warps 4-7   write an item's dQ (one query row per thread: TMEM ->
+//               16-bit -> a swizzled staging tile -> TMA store) while the
+//               next item accumulates in the other buffer.
 template <int D>
 struct DqGemmLayout {
   static constexpr int kStages = D > 64 ? 3 : 4;
@@ -946,17 +956,20 @@ struct DqGemmLayout {
   static constexpr uint32_t kKTile = kT * D * 2;     // K_j [128 keys][D]
   static constexpr uint32_t kStage = kDsTile + kKTile;
   static constexpr uint32_t RING = 0;
-  static constexpr uint32_t BAR = RING + kStages * kStage;
+  static constexpr uint32_t OUT = RING + kStages * kStage;  // dQ staging: D/64 swizzled [128][64] boxes
+  static constexpr uint32_t BAR = OUT + kT * D * 2;
   static constexpr int kFull = 0;                     // [kStages]
   static constexpr int kEmpty = kStages;              // [kStages]
-  static constexpr int kDone = 2 * kStages;
-  static constexpr int kDrain = 2 * kStages + 1;
-  static constexpr int kNumBars = 2 * kStages + 2;
+  static constexpr int kAccFull = 2 * kStages;        // [2] an item's last MMA done
+  static constexpr int kAccFree = 2 * kStages + 2;    // [2] the epilogue has read the accumulator
+  static constexpr int kDrain = 2 * kStages + 4;
+  static constexpr int kNumBars = 2 * kStages + 5;
   static constexpr uint32_t MISC = BAR + kNumBars * 8;
   static constexpr uint32_t kAlloc = MISC + 16 + 1024;
-  static constexpr uint32_t kCols = D;               // fp32 dQ accumulator columns
+  static constexpr uint32_t kCols = 2 * D;            // two fp32 dQ accumulators
+  static_assert(kAlloc <= 232448, "dQ GEMM shared memory exceeds the 227 KB per CTA");
 };
-constexpr int kDqGemmThreads = 128;
+constexpr int kDqGemmThreads = 256;  // warps 2-3 idle
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kDqGemmThreads, 1)
@@ -964,7 +977,7 @@ __global__ void __launch_bounds__(kDqGemmThreads, 1)
                    const __grid_constant__ CUtensorMap tmdq, T* __restrict__ dq, float scale,
                    MaskParams mp, const int32_t* __restrict__ row_ptr,
                    const int32_t* __restrict__ col_idx, const int32_t* __restrict__ csc_pos,
-                   int nnz, int heads, int kv_group, Strides3 sdq, int* status) {
+                   int nnz, int heads, int kv_group, int BH, Strides3 sdq, int* status) {
   using L = DqGemmLayout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = idesc_f16(kBF16, kT, D, true, true);  // M=128 q, N=D
@@ -979,51 +992,36 @@ __global__ void __launch_bounds__(kDqGemmThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ti = blockIdx.x;
-  const int bh = blockIdx.y;
-  const int hh = bh % heads, bb = bh / heads;
+  const int n_ti = ceil_div_dev(mp.n_q, kT);
   const int n_tj = ceil_div_dev(mp.n_kv, kT);
-  const PlanSpan span = plan_span(row_ptr, ti, n_tj, (int64_t)gridDim.x * n_tj, status);
-  const int e0 = span.e0;
-  const int nk = span.n;
-
-  if (nk == 0) {  // the tile's rows see no key: dQ = 0
-    for (int idx = threadIdx.x; idx < kT * (D / 8); idx += blockDim.x) {
-      const int rr = idx / (D / 8), cc = idx % (D / 8);
-      const int row = ti * kT + rr;
-      if (row < mp.n_q)
-        reinterpret_cast<uint4*>(dq + bb * sdq.b + hh * sdq.h + (int64_t)row * sdq.n)[cc] =
-            make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
-
-  const int64_t tile0 = (int64_t)bh * nnz;   // this query (b, h)'s first stored dS tile
-  // (dS_ij^T, K_j) of CSR entry e0 + p into ring stage p % kStages
-  auto load = [&](int p) {
-    const int s = p % L::kStages;
-    const int kt = plan_index(plan_entry(col_idx, e0 + p, n_tj, status));
-    const int cp = bounded(__ldg(csc_pos + e0 + p), nnz, status);
-    const uint32_t dst = sb + L::RING + (uint32_t)s * L::kStage;
-    mbar_expect_tx(bar(L::kFull + s), L::kStage);
-    bulk_load(dst, ds + (size_t)(tile0 + cp) * (kT * kT), L::kDsTile, bar(L::kFull + s));
-    for (int b = 0; b < kBoxes; ++b)
-      tma_load_4d(dst + L::kDsTile + (uint32_t)b * 16384u, &tmk, bar(L::kFull + s), 64 * b,
-                  kt * kT, hh / kv_group, bb);
+  const int n_items = n_ti * BH;
+  // item it: query tile ti of query (b, h) bh, the kept key tiles
+  // [e0, e0 + nk) of its CSR row
+  struct Item {
+    int ti, bh, e0, nk;
   };
-  const int first = min(nk, L::kStages);
+  auto item = [&](int it) -> Item {
+    Item w;
+    w.bh = it / n_ti;
+    w.ti = it - w.bh * n_ti;
+    const PlanSpan span = plan_span(row_ptr, w.ti, n_tj, (int64_t)n_ti * n_tj, status);
+    w.e0 = span.e0;
+    w.nk = span.n;
+    return w;
+  };
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::kStages; ++s) {
       mbar_init(bar(L::kFull + s), 1);
       mbar_init(bar(L::kEmpty + s), 1);
     }
-    mbar_init(bar(L::kDone), 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar(L::kAccFull + a), 1);
+      mbar_init(bar(L::kAccFree + a), 128);
+    }
     mbar_init(bar(L::kDrain), 1);
     *abort_flag = 0;
     mbar_init_fence();
-    // the first stages are requested before the TMEM allocation and the
-    // CTA-wide sync, so their latency overlaps them
-    for (int p = 0; p < first; ++p) load(p);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::kCols);
@@ -1034,82 +1032,133 @@ __global__ void __launch_bounds__(kDqGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  bool ok = true;
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    int issued = first;
     if (lane == 0) {
-      for (int p = first; p < nk; ++p) {
-        const int s = p % L::kStages, f = p / L::kStages;
-        if (!wait_bar(bar(L::kEmpty + s), (uint32_t)((f - 1) & 1), abort_flag, status)) break;
-        load(p);
-        issued = p + 1;
+      uint32_t gp = 0;  // (dS, K) pairs loaded by this CTA so far
+      bool run = true;
+      for (int it = blockIdx.x; run && it < n_items; it += gridDim.x) {
+        const Item w = item(it);
+        const int hh = w.bh % heads, bb = w.bh / heads;
+        const int64_t tile0 = (int64_t)w.bh * nnz;  // the query (b, h)'s first stored dS tile
+        for (int p = 0; p < w.nk; ++p, ++gp) {
+          const uint32_t s = gp % L::kStages, f = gp / L::kStages;
+          if (f > 0 && !wait_bar(bar(L::kEmpty + s), (f - 1) & 1u, abort_flag, status)) {
+            run = false;
+            break;
+          }
+          const int kt = plan_index(plan_entry(col_idx, w.e0 + p, n_tj, status));
+          const int cp = bounded(__ldg(csc_pos + w.e0 + p), nnz, status);
+          const uint32_t dst = sb + L::RING + s * L::kStage;
+          mbar_expect_tx(bar(L::kFull + s), L::kStage);
+          bulk_load(dst, ds + (size_t)(tile0 + cp) * (kT * kT), L::kDsTile, bar(L::kFull + s));
+          for (int b = 0; b < kBoxes; ++b)
+            tma_load_4d(dst + L::kDsTile + (uint32_t)b * 16384u, &tmk, bar(L::kFull + s), 64 * b,
+                        kt * kT, hh / kv_group, bb);
+        }
       }
       // every copy this thread issued lands before the CTA can exit
-      for (int s = 0; s < L::kStages; ++s) {
-        const int fills = issued > s ? (issued - 1 - s) / L::kStages + 1 : 0;
-        if (fills) wait_bar_drain(bar(L::kFull + s), (uint32_t)((fills - 1) & 1), status);
+      for (uint32_t s = 0; s < (uint32_t)L::kStages; ++s) {
+        const uint32_t fills = gp > s ? (gp - 1 - s) / L::kStages + 1 : 0;
+        if (fills) wait_bar_drain(bar(L::kFull + s), (fills - 1) & 1u, status);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    for (int p = 0; p < nk; ++p) {
-      const int s = p % L::kStages;
-      if (!wait_bar_w(bar(L::kFull + s), (uint32_t)((p / L::kStages) & 1), abort_flag, status))
+    uint32_t gc = 0;  // pairs consumed
+    uint32_t ai = 0;  // items accumulated (items with no kept tile take no buffer)
+    bool run = true;
+    for (int it = blockIdx.x; run && it < n_items; it += gridDim.x) {
+      const Item w = item(it);
+      if (w.nk == 0) continue;
+      const uint32_t a = ai & 1u;
+      if (ai >= 2 && !wait_bar_w(bar(L::kAccFree + a), ((ai >> 1) - 1) & 1u, abort_flag, status))
         break;
       tc_fence_after();
-      // A: 16 keys per k-step = ds_tile_offset(0, 16 kk); core matrices 128 B
-      // apart along the keys, 2048 B apart along the queries
-      const uint64_t da =
-          smem_desc_noswizzle(sb + L::RING + (uint32_t)s * L::kStage, 128u, kDsChunkBytes);
-      const uint64_t db = desc_mnmajor(sb + L::RING + (uint32_t)s * L::kStage + L::kDsTile, 16384u);
+      const uint32_t acc = tmem + a * (uint32_t)D;
+      for (int p = 0; p < w.nk; ++p, ++gc) {
+        const uint32_t s = gc % L::kStages;
+        if (!wait_bar_w(bar(L::kFull + s), (gc / L::kStages) & 1u, abort_flag, status)) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        // A: 16 keys per k-step = ds_tile_offset(0, 16 kk); core matrices 128 B
+        // apart along the keys, 2048 B apart along the queries
+        const uint64_t da = smem_desc_noswizzle(sb + L::RING + s * L::kStage, 128u, kDsChunkBytes);
+        const uint64_t db = desc_mnmajor(sb + L::RING + s * L::kStage + L::kDsTile, 16384u);
 #pragma unroll
-      for (int kk = 0; kk < kT / 16; ++kk)
-        mma_f16_ss_w(tmem, desc_advance(da, ds_tile_offset(0, 16 * kk)),
-                     desc_advance(db, (uint32_t)kk * 2048u), kIdesc, (p > 0 || kk > 0) ? 1u : 0u);
-      tc_commit_w(bar(L::kEmpty + s));
+        for (int kk = 0; kk < kT / 16; ++kk)
+          mma_f16_ss_w(acc, desc_advance(da, ds_tile_offset(0, 16 * kk)),
+                       desc_advance(db, (uint32_t)kk * 2048u), kIdesc,
+                       (p > 0 || kk > 0) ? 1u : 0u);
+        tc_commit_w(bar(L::kEmpty + s));
+      }
+      if (!run) break;
+      tc_commit_w(bar(L::kAccFull + a));
+      ++ai;
     }
-    tc_commit_w(bar(L::kDone));
     tc_commit_w(bar(L::kDrain));
     wait_bar_drain(bar(L::kDrain), 0, status);
-  }
-
-  // ---------------------------------------------------------------- epilogue
-  // thread r holds query row r of dQ; staged in ring stage 0's dS buffer
-  // (free once every MMA is done) as D/64 swizzled [128][64] boxes
-  ok = wait_bar(bar(L::kDone), 0, abort_flag, status) && !*abort_flag;
-  ok = __syncthreads_and(ok ? 1 : 0) != 0;
-  if (ok) {
-    tc_fence_after();
-    const int r = threadIdx.x;
-    const uint32_t t_acc = tmem + ((uint32_t)(warp * 32) << 16);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    // thread r holds query row r of the item's dQ: TMEM -> 16-bit registers
+    // (the accumulator is then released to the MMA warp) -> the staging tile
+    // as D/64 swizzled [128][64] boxes -> TMA store, which overlaps the next
+    // item's accumulation
+    const int r = threadIdx.x - 128;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    uint32_t ai = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const Item w = item(it);
+      const int hh = w.bh % heads, bb = w.bh / heads;
+      if (w.nk == 0) {  // the tile's rows see no key: dQ = 0
+        const int row = w.ti * kT + r;
+        if (row < mp.n_q) {
+          uint4* dst = reinterpret_cast<uint4*>(dq + bb * sdq.b + hh * sdq.h + (int64_t)row * sdq.n);
+          for (int cc = 0; cc < D / 8; ++cc) dst[cc] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      const uint32_t a = ai & 1u;
+      bool ok = wait_bar(bar(L::kAccFull + a), (ai >> 1) & 1u, abort_flag, status);
+      if (!named_bar_and(1, 128, ok && !*abort_flag)) break;
+      tc_fence_after();
+      uint32_t packed[D / 2];
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t t[32];
-      tmem_ld32(t_acc + 32u * c, t);
-      tmem_wait_ld();
-      uint32_t w[16];
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(tmem + lane_base + a * (uint32_t)D + 32u * c, t);
+        tmem_wait_ld();
 #pragma unroll
-      for (int i2 = 0; i2 < 16; ++i2)
-        w[i2] = pack2<T>(__uint_as_float(t[2 * i2]) * scale, __uint_as_float(t[2 * i2 + 1]) * scale);
-      const uint32_t region = sb + L::RING + (uint32_t)((32 * c) >> 6) * 16384u;
+        for (int i2 = 0; i2 < 16; ++i2)
+          packed[16 * c + i2] =
+              pack2<T>(__uint_as_float(t[2 * i2]) * scale, __uint_as_float(t[2 * i2 + 1]) * scale);
+      }
+      tc_fence_before();
+      mbar_arrive(bar(L::kAccFree + a));
+      // the previous item's store has finished reading the staging tile
+      if (r == 0) bulk_wait_read0();
+      named_bar_sync(1, 128);
 #pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2) {
-        const uint32_t addr = region + sw128_offset((uint32_t)r, (uint32_t)((32 * c) & 63) + 8u * i2);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * i2]),
-                     "r"(w[4 * i2 + 1]), "r"(w[4 * i2 + 2]), "r"(w[4 * i2 + 3])
+      for (int c = 0; c < D / 8; ++c) {
+        const uint32_t addr = sb + L::OUT + (uint32_t)(c >> 3) * 16384u +
+                              sw128_offset((uint32_t)r, (uint32_t)(8 * c) & 63u);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * c]),
+                     "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
                      : "memory");
       }
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (r == 0) {
+        for (int b = 0; b < kBoxes; ++b)
+          tma_store_4d(&tmdq, sb + L::OUT + (uint32_t)b * 16384u, 64 * b, w.ti * kT, hh, bb);
+        bulk_commit();
+      }
+      ++ai;
     }
-    fence_proxy_async_smem();
-    named_bar_sync(1, kDqGemmThreads);
-    if (threadIdx.x == 0) {
-      for (int b = 0; b < kBoxes; ++b)
-        tma_store_4d(&tmdq, sb + L::RING + (uint32_t)b * 16384u, 64 * b, ti * kT, hh, bb);
-      bulk_commit();
-      bulk_wait_read0();
-    }
+    if (r == 0) bulk_wait_read0();
   }
   tc_fence_before();
   __syncthreads();
@@ -1180,12 +1229,13 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
                                                  (int)L::kAlloc),
                             "cudaFuncSetAttribute(dq_gemm)"))
       return rc;
-    dim3 grid(ceil_div_i(mp.n_q, kT), BH);
+    // persistent: one CTA per SM over the (query tile, query (b, h)) items
+    const int64_t items = (int64_t)ceil_div_i(mp.n_q, kT) * BH;
+    const int grid = (int)std::min<int64_t>(items, device_sm_count());
     LaunchScope ls("dq_gemm_kernel", s);
     kern<<<grid, kDqGemmThreads, L::kAlloc, s>>>((const T*)ds_ws, mk, mdq, (T*)dq, scale, mp,
-                                                 dq_rp, dq_ci,
-                                                 csc_pos, nnz, vw.heads, vw.kv_group, vw.dq,
-                                                 status);
+                                                 dq_rp, dq_ci, csc_pos, nnz, vw.heads,
+                                                 vw.kv_group, BH, vw.dq, status);
     return check_launch("dq_gemm_kernel");
   }
   {
