@@ -9,7 +9,9 @@ no key scattered between the others (items that take no accumulator), so
 every CTA crosses item boundaries, reuses both accumulators and its staging
 tile, and skips empty items.  Each head's O and dQ must equal, bit for bit,
 the same head run alone (one item per CTA); two heads are also checked
-against the float64 oracle, gradients included.
+against the float64 oracle, gradients included.  At head_dim 64 the backward
+recomputes dQ (``dq_tc_kernel``) instead of storing dS, so that case checks
+the same properties on the non-persistent kernels.
 """
 
 from __future__ import annotations
