@@ -19,8 +19,10 @@ The K timed fwd+bwd steps are replays of the step captured once into a
 CUDA graph (the same kernels; the host queues the whole timed region at
 once, so a stalled host thread cannot idle the GPU); an eager timed pass of
 the same step follows and is reported in ``extra.fwdbwd.eager_pass``.
-``e2e`` runs the same step through the public API from pinned host buffers
-(Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step).
+``e2e`` runs the same step K times through the public API from pinned host
+buffers (Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step;
+copies in, compute and copies out on three streams, two steps in flight) and
+reports each stage's median device time.
 ``roofline`` uses the dominant kernel's duration measured in the eager timed
 pass with CUDA events recorded by libsbfa around each launch.
 ``--impl reference`` times the upstream eager masked-attention algorithm
@@ -34,6 +36,7 @@ import datetime
 import json
 import math
 import os
+import statistics
 import subprocess
 import sys
 import time
@@ -413,24 +416,36 @@ def make_inputs(cfg, seed: int, n_q=None, local=None):
 def e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, steps: int, warmup: int):
     """Milliseconds for `steps` end-to-end fwd+bwd steps (max over ranks):
     copy-in on one stream, compute on the current stream, copy-out on a
-    third, with events ordering the reuse of the two buffer sets."""
+    third, with events ordering the reuse of the two buffer sets.  Also
+    returns the median device time of each stage over the timed steps (rank
+    0's), which shows which of the three bounds the pipeline.  The garbage
+    collector is paused over the timed steps."""
+    import gc
     comp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_comp = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def run(n, start_ev):
+    def run(n, start_ev, stages=None):
         for i in range(n):
             b = i % 2
+            st = None if stages is None else [torch.cuda.Event(enable_timing=True)
+                                              for _ in range(6)]
             with torch.cuda.stream(s_in):
                 s_in.wait_event(start_ev)
                 if i >= 2:
                     s_in.wait_event(ev_comp[b])  # step i-2 has finished reading dev_in[b]
+                if st:
+                    st[0].record(s_in)
                 for d, h in zip(dev_in[b], host_in):
                     d.copy_(h, non_blocking=True)
+                if st:
+                    st[1].record(s_in)
                 ev_in[b].record(s_in)
             comp.wait_event(ev_in[b])
+            if st:
+                st[2].record(comp)
             qd, kd, vd, dod = dev_in[b]
             for t in (qd, kd, vd):
                 t.requires_grad_(True)
@@ -438,13 +453,21 @@ def e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, steps: int, warmu
             o = stk.block_sparse_attention(qd, kd, vd, mask, **kw)
             o.backward(dod)
             outs = (o.detach(), qd.grad, kd.grad, vd.grad)
+            if st:
+                st[3].record(comp)
             ev_comp[b].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_comp[b])
+                if st:
+                    st[4].record(s_out)
                 for h, d in zip(out_h[b], outs):
                     h.copy_(d, non_blocking=True)
                     d.record_stream(s_out)
+                if st:
+                    st[5].record(s_out)
                 ev_out[b].record(s_out)
+            if st:
+                stages.append(st)
             for t in (qd, kd, vd):
                 t.grad = None
                 t.requires_grad_(False)
@@ -458,12 +481,23 @@ def e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, steps: int, warmu
     torch.cuda.synchronize()
     dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(comp)
-    run(steps, start)
-    end.record(comp)
-    torch.cuda.synchronize()
+    stages = []
+    gc.collect()
+    gc.disable()
+    try:
+        start.record(comp)
+        run(steps, start, stages)
+        end.record(comp)
+        torch.cuda.synchronize()
+    finally:
+        gc.enable()
     dist.barrier()
-    return dist.max(start.elapsed_time(end))
+
+    def med(a, b):
+        return round(statistics.median(st[a].elapsed_time(st[b]) for st in stages), 3)
+
+    stage_ms = {"h2d": med(0, 1), "compute": med(2, 3), "d2h": med(4, 5)}
+    return dist.max(start.elapsed_time(end)), stage_ms
 
 
 def local_units(dist, cfg):
@@ -578,17 +612,19 @@ def bench_fwdbwd(dist, args, pk, src):
     out_h = [[torch.empty(q.shape, dtype=cfg["dtype"]).pin_memory() for _ in range(4)]
              for _ in range(2)]
     dev_in = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
-    e_steps = max(2, min(args.steps, 5))
-    e_ms = float("nan")
+    e_steps = max(2, args.steps)
+    e_ms, e_stages = float("nan"), None
     if not args.no_e2e:
-        e_ms = e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, e_steps, warmup=2)
+        e_ms, e_stages = e2e_pipelined(dist, stk, mask, kw, host_in, dev_in, out_h, e_steps,
+                                       warmup=2)
     bytes_h2d = sum(t.numel() * t.element_size() for t in host_in)
     bytes_d2h = sum(t.numel() * t.element_size() for t in out_h[0])
     e2e = None if args.no_e2e else {
         "value": round(3.5 * F * e_steps / (e_ms / 1e3) / 1e12, 3),
         "unit": "TFLOP/s", "h2d_bytes_per_step": bytes_h2d * dist.world,
         "d2h_bytes_per_step": bytes_d2h * dist.world,
-        "ms_per_step": round(e_ms / e_steps, 3),
+        "ms_per_step": round(e_ms / e_steps, 3), "steps": e_steps,
+        "stage_ms_median_rank0": e_stages,
         "pipeline": "copy-in / compute / copy-out on three streams, two steps in flight"}
     if e2e is not None:
         e2e["copies"] = copy_peaks(dist, host_in, dev_in[0], out_h[0], e_ms / e_steps)
