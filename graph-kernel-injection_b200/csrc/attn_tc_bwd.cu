@@ -26,7 +26,11 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
 #include <type_traits>
+#include <utility>
+#include <vector>
 
 #include "tc_attn_common.cuh"
 
@@ -1168,13 +1172,19 @@ __global__ void __launch_bounds__(kDqGemmThreads, 1)
   }
 }
 
+// Integer tuning knob from the environment (dflt when unset or empty).
+int env_int(const char* name, int dflt) {
+  const char* e = std::getenv(name);
+  return e != nullptr && *e != '\0' ? std::atoi(e) : dflt;
+}
+
 template <typename T, int D>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq,
                   void* dk, void* dv, const float* lse, const float* delta, int BH, float scale,
                   const MaskParams& mp, const Views& vw, const int32_t* dq_rp,
                   const int32_t* dq_ci, const int32_t* kv_cp, const int32_t* kv_ri,
                   float* part_ws, int sink_parts, const int32_t* csc_pos, int nnz, void* ds_ws,
-                  int* status, cudaStream_t s) {
+                  int* status, cudaStream_t s, cudaStream_t s_dq = nullptr, int dq_grid = 0) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   const uint64_t nq = (uint64_t)mp.n_q, nkv = (uint64_t)mp.n_kv;
@@ -1229,14 +1239,46 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
                                                  (int)L::kAlloc),
                             "cudaFuncSetAttribute(dq_gemm)"))
       return rc;
-    // persistent: one CTA per SM over the (query tile, query (b, h)) items
+    // on the side stream when given: it waits for this call's dK/dV pass
+    // and then runs beside the next group's
+    cudaStream_t sq = s;
+    if (s_dq != nullptr && s_dq != s) {
+      cudaEvent_t ev = nullptr;
+      if (int rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming),
+                              "cudaEventCreateWithFlags"))
+        return rc;
+      cudaError_t e = cudaEventRecord(ev, s);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s_dq, ev, 0);
+      cudaEventDestroy(ev);
+      if (int rc = check_cuda(e, "dQ side stream: wait for the dK/dV pass")) return rc;
+      sq = s_dq;
+    }
+    // persistent: one CTA per SM (or dq_grid CTAs) over the (query tile,
+    // query (b, h)) items
     const int64_t items = (int64_t)ceil_div_i(mp.n_q, kT) * BH;
-    const int grid = (int)std::min<int64_t>(items, device_sm_count());
-    LaunchScope ls("dq_gemm_kernel", s);
-    kern<<<grid, kDqGemmThreads, L::kAlloc, s>>>((const T*)ds_ws, mk, mdq, (T*)dq, scale, mp,
-                                                 dq_rp, dq_ci, csc_pos, nnz, vw.heads,
-                                                 vw.kv_group, BH, vw.dq, status);
-    return check_launch("dq_gemm_kernel");
+    const int cap = dq_grid > 0 ? std::min(dq_grid, device_sm_count()) : device_sm_count();
+    const int grid = (int)std::min<int64_t>(items, cap);
+    LaunchScope ls("dq_gemm_kernel", sq);
+    // the priority travels with the launch itself, so a captured CUDA graph
+    // keeps it too
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kDqGemmThreads);
+    cfg.dynamicSmemBytes = L::kAlloc;
+    cfg.stream = sq;
+    cudaLaunchAttribute attr[1];
+    int least = 0, greatest = 0;
+    if (sq != s && env_int("SBFA_DQ_PRIO", 1) != 0 &&
+        cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess) {
+      attr[0].id = cudaLaunchAttributePriority;
+      attr[0].val.priority = greatest;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, (const T*)ds_ws, mk, mdq, (T*)dq, scale, mp,
+                                         dq_rp, dq_ci, csc_pos, nnz, vw.heads, vw.kv_group, BH,
+                                         vw.dq, status),
+                      "dq_gemm_kernel");
   }
   {
     using L = DqLayout<D>;
@@ -1252,6 +1294,101 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
                                               status);
   }
   return check_launch("dq_tc_kernel");
+}
+
+
+// Side stream for the dQ GEMM of calls on caller stream `s`: one per (device,
+// caller stream), created on first use at the highest priority, so that the
+// GEMM's CTAs take SMs as the dK/dV pass frees them.  Calls on different
+// caller streams never share a side stream (a CUDA-graph capture of one
+// caller stream takes in only its own).  nullptr (no overlap) past 64 caller
+// streams or when creation fails.
+cudaStream_t dq_side_stream(cudaStream_t s) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, cudaStream_t>, cudaStream_t>> table;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& e : table)
+    if (e.first.first == dev && e.first.second == s) return e.second;
+  if (table.size() >= 64) return nullptr;
+  int least = 0, greatest = 0;
+  if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) greatest = 0;
+  cudaStream_t st = nullptr;
+  if (cudaStreamCreateWithPriority(&st, cudaStreamNonBlocking, greatest) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  table.push_back({{dev, s}, st});
+  return st;
+}
+
+// The backward over the stored dS, overlapped: the (b, h) units are cut into
+// groups (whole batch elements, or head ranges of one when there are fewer
+// batch elements than groups); group g's dK/dV pass runs on the caller's
+// stream and its dQ GEMM, an HBM-bound kernel, on the side stream beside the
+// tensor-bound dK/dV pass of group g + 1, on 3/8 of the SMs (the last
+// group's on all of them, with nothing left to overlap).  Every group reads
+// and writes only its own rows, so the order between groups does not matter;
+// the caller's stream waits for the side stream before it returns, and a
+// CUDA-graph capture of the caller's stream takes the side stream in and
+// joins it again.  Four groups once the problem has at least 16 items per SM
+// (below that the extra launches cost more than the overlap gains);
+// SBFA_BWD_GROUPS and SBFA_DQ_GRID override the group count and the dQ
+// GEMM's CTA count (SBFA_BWD_GROUPS=1: one dK/dV pass, then dQ on the
+// caller's stream).
+template <typename T, int D>
+int run_bwd_tc(const void* q, const void* k, const void* v, const void* dout, void* dq, void* dk,
+               void* dv, const float* lse, const float* delta, int BH, float scale,
+               const MaskParams& mp, const Views& vw, const int32_t* dq_rp, const int32_t* dq_ci,
+               const int32_t* kv_cp, const int32_t* kv_ri, float* part_ws, int sink_parts,
+               const int32_t* csc_pos, int nnz, void* ds_ws, int* status, cudaStream_t s) {
+  const int sms = device_sm_count();
+  const int64_t items = (int64_t)ceil_div_i(mp.n_q, kT) * BH;
+  int want = env_int("SBFA_BWD_GROUPS", 0);
+  if (want <= 0) want = items >= 16LL * sms ? 4 : 1;
+  int dq_grid = env_int("SBFA_DQ_GRID", 0);
+  if (dq_grid <= 0) dq_grid = std::max(1, sms * 3 / 8);
+  const int H = vw.heads, B = BH / H, g = vw.kv_group;
+  cudaStream_t side = ds_ws != nullptr && want > 1 ? dq_side_stream(s) : nullptr;
+  if (side == nullptr)
+    return launch_bwd_tc<T, D>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw, dq_rp,
+                               dq_ci, kv_cp, kv_ri, part_ws, sink_parts, csc_pos, nnz, ds_ws,
+                               status, s);
+  int hsplit = std::max(1, want / std::max(B, 1));
+  while (hsplit > 1 && (H % hsplit != 0 || (H / hsplit) % g != 0)) --hsplit;
+  const int Hg = H / hsplit;
+  Views vg = vw;
+  vg.heads = Hg;
+  const int64_t es = (int64_t)sizeof(T);
+  for (int bi = 0; bi < B; ++bi) {
+    for (int hs = 0; hs < hsplit; ++hs) {
+      const int h0 = hs * Hg;
+      const int64_t u = (int64_t)bi * H + h0;  // the group's first query (b, h)
+      auto qo = [&](const Strides3& st) { return (bi * st.b + (int64_t)h0 * st.h) * es; };
+      auto ko = [&](const Strides3& st) { return (bi * st.b + (int64_t)(h0 / g) * st.h) * es; };
+      const bool last = bi == B - 1 && hs == hsplit - 1;
+      if (int rc = launch_bwd_tc<T, D>(
+              static_cast<const char*>(q) + qo(vw.q), static_cast<const char*>(k) + ko(vw.k),
+              static_cast<const char*>(v) + ko(vw.v), static_cast<const char*>(dout) + qo(vw.dout),
+              static_cast<char*>(dq) + qo(vw.dq), static_cast<char*>(dk) + ko(vw.dk),
+              static_cast<char*>(dv) + ko(vw.dv), lse + u * mp.n_q, delta + u * mp.n_q, Hg, scale,
+              mp, vg, dq_rp, dq_ci, kv_cp, kv_ri,
+              part_ws != nullptr ? part_ws + (u / g) * sink_parts * 2 * kT * D : nullptr,
+              sink_parts, csc_pos, nnz,
+              static_cast<char*>(ds_ws) + u * nnz * (int64_t)(kT * kT * 2), status, s, side,
+              last ? 0 : dq_grid))
+        return rc;
+    }
+  }
+  cudaEvent_t ev = nullptr;
+  if (int rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming),
+                          "cudaEventCreateWithFlags"))
+    return rc;
+  cudaError_t e = cudaEventRecord(ev, side);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev, 0);
+  cudaEventDestroy(ev);
+  return check_cuda(e, "dQ side stream: join");
 }
 
 }  // namespace
@@ -1296,9 +1433,9 @@ int tc_bwd(int dtype, int D, const void* q, const void* k, const void* v, const 
                       ds_ws_bytes >= ds_need && ((uintptr_t)ds_ws & 15u) == 0;
   void* dsw = use_ds ? ds_ws : nullptr;
   const int nz = use_ds ? (int)nnz : 0;
-#define SBFA_BWD(TT, DD)                                                                        \
-  return launch_bwd_tc<TT, DD>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw, dq_rp, \
-                               dq_ci, kv_cp, kv_ri, part, parts, csc_pos, nz, dsw, status, s)
+#define SBFA_BWD(TT, DD)                                                                       \
+  return run_bwd_tc<TT, DD>(q, k, v, dout, dq, dk, dv, lse, delta, BH, scale, mp, vw, dq_rp,  \
+                            dq_ci, kv_cp, kv_ri, part, parts, csc_pos, nz, dsw, status, s)
   if (D == 128) {
     if (bf) SBFA_BWD(__nv_bfloat16, 128);
     SBFA_BWD(__half, 128);

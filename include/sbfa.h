@@ -192,7 +192,16 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
  * stores every 16-bit dS tile there and dQ becomes a GEMM over the stored
  * tiles, instead of a third pass that recomputes S, P and dP; NULL keeps that
  * pass.  The two give the same dQ to rounding (the dS values are the dK/dV
- * pass's). */
+ * pass's).  With the stored tiles and a large enough problem (16 or more
+ * 128-row query tiles x B*H per SM) the dQ GEMM of one group of (b, h) units
+ * runs on a library-owned high-priority side stream beside the next group's
+ * dK/dV pass; the side stream belongs to `stream` (one per device and
+ * caller stream), waits on it through events and is joined back into it
+ * before the call returns, so work queued after the call, and a CUDA-graph
+ * capture of `stream`, see one stream.  Results are bit-identical with and
+ * without the overlap.  Environment: SBFA_BWD_GROUPS=n forces n groups (1
+ * switches the overlap off), SBFA_DQ_GRID=n the dQ GEMM's CTA count while
+ * it overlaps (default 3/8 of the SMs). */
 int sbfa_bwd(const void* q, const void* k, const void* v, const void* o,
              const float* lse, const void* dout, void* dq, void* dk, void* dv,
              float* delta_ws, int64_t B, int64_t H, int64_t n_q, int64_t n_kv,
