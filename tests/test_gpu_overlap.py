@@ -84,7 +84,10 @@ def test_overlapped_backward_bitwise(groups_env, B, H, kv_heads, groups):
         check_half(got[2][:1, :1], r[2], torch.bfloat16, "dK head 0 vs oracle")
 
 
-def test_overlapped_backward_in_cuda_graph(groups_env):
+@pytest.mark.parametrize("mode", ["thread_local", "global"])
+def test_overlapped_backward_in_cuda_graph(groups_env, mode):
+    """The capture runs on a stream no backward call has used before, so
+    the backward creates that stream's side stream inside the capture."""
     B, H, N, S, W = 2, 8, 2048, 4, 512
     os.environ["SBFA_BWD_GROUPS"] = "4"
     q0, k0, v0, do = _inputs(B, H, H, N, seed=5)
@@ -107,7 +110,7 @@ def test_overlapped_backward_in_cuda_graph(groups_env):
         step()
     torch.cuda.current_stream().wait_stream(side)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(), capture_error_mode=mode):
         o_g = step()
     for _ in range(2):
         graph.replay()
