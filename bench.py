@@ -23,8 +23,11 @@ the same step follows and is reported in ``extra.fwdbwd.eager_pass``.
 buffers (Q, K, V, dO host->device, O, dQ, dK, dV device->host, every step;
 copies in, compute and copies out on three streams, two steps in flight) and
 reports each stage's median device time.
-``roofline`` uses the dominant kernel's duration measured in the eager timed
-pass with CUDA events recorded by libsbfa around each launch.
+``roofline`` uses the dominant kernel's device time per step, from CUDA
+events recorded by libsbfa around each launch in a further eager timed pass
+with the dQ GEMM serialised after one dK/dV pass (SBFA_BWD_GROUPS=1), so
+each kernel's duration is its own; the same figure for the overlapped eager
+pass is ``extra.fwdbwd.roofline_overlapped_pass``.
 ``--impl reference`` times the upstream eager masked-attention algorithm
 (the CPU oracle port) on the host cores instead.
 """
@@ -342,17 +345,20 @@ def tensor_peak(pk, clocks):
     return pk["bf16_tflops"], "burst"
 
 
-def roofline(per_kernel, flops_fwd, pk, peak_src, clocks=None, kv_bytes=None, workload="",
-             scale_units=1.0):
-    """Roofline of the dominant kernel.  flops_fwd / kv_bytes are this
-    rank's algorithmic work per step; `traffic` is the committed ncu DRAM
-    byte count of one full-size launch scaled by this rank's share of the
-    (batch, head) units."""
+def roofline(per_kernel, flops_fwd, pk, peak_src, steps, clocks=None, kv_bytes=None,
+             workload="", scale_units=1.0):
+    """Roofline of the dominant kernel over `steps` timed steps.  flops_fwd /
+    kv_bytes are this rank's algorithmic work per step, and `achieved`
+    divides the kernel's share of it by the kernel's device time per step
+    (the sum of its launches: the backward launches dK/dV and the dQ GEMM
+    once per group of (b, h) units when it overlaps them); `traffic` is the
+    committed ncu DRAM byte count of the kernel's work in one full-size step,
+    scaled by this rank's share of the (batch, head) units."""
     if not per_kernel:
         return None
     name, (tot, cnt) = max(per_kernel.items(), key=lambda kv: kv[1][0])
     kind = kernel_kind(name)
-    avg_s = tot / cnt / 1e3
+    avg_s = tot / steps / 1e3
     if kind == "decode":
         achieved = kv_bytes / avg_s / 1e9   # one split launch reads every visible K/V row once
         peak, which = pk["hbm_gbs"], "HBM copy"
@@ -372,7 +378,8 @@ def roofline(per_kernel, flops_fwd, pk, peak_src, clocks=None, kv_bytes=None, wo
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
             "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_source": f"{peak_src} ({which})",
-            "avg_launch_ms": round(tot / cnt, 4), "launches": cnt,
+            "ms_per_step": round(tot / steps, 4), "avg_launch_ms": round(tot / cnt, 4),
+            "launches": cnt,
             "kernel_share": {k: round(v[0] / sum(x[0] for x in per_kernel.values()), 4)
                              for k, v in per_kernel.items()}}
 
@@ -577,6 +584,19 @@ def bench_fwdbwd(dist, args, pk, src):
     if gres is None:
         ms, launches, clk = e_ms, e_launches, eclk
         step_ms, host_ms = list(STEP_MS), list(HOST_MS)
+    # roofline pass: with the dQ GEMM overlapped, dK/dV and dQ share the SMs
+    # and each one's CUDA-event duration includes the other's; this eager
+    # pass runs one dK/dV pass and then the dQ GEMM, so each duration is the
+    # kernel's own (the shares then compare with ncu's serialised launches)
+    old_groups = os.environ.get("SBFA_BWD_GROUPS")
+    os.environ["SBFA_BWD_GROUPS"] = "1"
+    try:
+        _, _, per_kernel_iso = time_steps(dist, step, args.steps, args.warmup)
+    finally:
+        if old_groups is None:
+            os.environ.pop("SBFA_BWD_GROUPS", None)
+        else:
+            os.environ["SBFA_BWD_GROUPS"] = old_groups
     else:
         ms, launches = gres["ms"], gres["launches"]
         step_ms, host_ms = gres["step_ms"], gres["host_ms"]
@@ -629,9 +649,15 @@ def bench_fwdbwd(dist, args, pk, src):
     if e2e is not None:
         e2e["copies"] = copy_peaks(dist, host_in, dev_in[0], out_h[0], e_ms / e_steps)
     del dev_in, hq, hk, hv, hdo, host_in, out_h
-    rl = roofline(per_kernel, F_local, pk, src, clocks=clk, workload="cfg2",
+    rl_ovl = roofline(per_kernel, F_local, pk, src, args.steps, clocks=clk, workload="cfg2",
+                      scale_units=(stop - start) / units)
+    rl = roofline(per_kernel_iso, F_local, pk, src, args.steps, clocks=clk, workload="cfg2",
                   scale_units=(stop - start) / units)
+    if rl is not None:
+        rl["timed_as"] = ("eager pass with the dQ GEMM after one dK/dV pass "
+                          "(SBFA_BWD_GROUPS=1), so each kernel's duration is its own")
     res = dict(value=value, ms=ms, launches=launches, clocks=clk, e2e=e2e, roofline=rl,
+               roofline_overlapped=rl_ovl, per_kernel_iso=per_kernel_iso,
                nnz=nnz, flops_fwd=F, verify=verify, per_kernel=per_kernel, step_ms=step_ms,
                host_ms=host_ms, eager=eager,
                timing=("CUDA-graph replays of the captured fwd+bwd step" if gres is not None
@@ -736,7 +762,8 @@ def bench_fwd(dist, args, pk, src):
     clk = clocks.stop(WINDOW)
     value = F * steps / (ms / 1e3) / 1e12
     share = (stop - start) / units
-    rl = roofline(per_kernel, F * share, pk, src, clocks=clk, workload="cfg3", scale_units=share)
+    rl = roofline(per_kernel, F * share, pk, src, steps, clocks=clk, workload="cfg3",
+                  scale_units=share)
     del q, k, v
     torch.cuda.empty_cache()
     return dict(value=value, ms=ms / steps, roofline=rl, nnz=nnz, launches=launches, clocks=clk,
@@ -777,7 +804,7 @@ def bench_decode(dist, args, pk, src):
     steps = max(5, args.steps * 5)
     ms, launches, per_kernel = time_steps(dist, step, steps, args.warmup)
     value = kv_bytes * steps / (ms / 1e3) / 1e9
-    rl = roofline(per_kernel, 0.0, pk, src, kv_bytes=kv_bytes * share, workload="cfg4",
+    rl = roofline(per_kernel, 0.0, pk, src, steps, kv_bytes=kv_bytes * share, workload="cfg4",
                   scale_units=share)
 
     # the same decode over a StreamingLLM ring cache holding sink + window rows
@@ -800,7 +827,7 @@ def bench_decode(dist, args, pk, src):
     gqa = {"value": round(g_bytes * steps / (g_ms / 1e3) / 1e9, 2), "unit": "GB/s",
            "ms_per_step": round(g_ms / steps, 4), "kv_heads_per_query_heads": f"1/{gq}",
            "kv_bytes_per_step": int(g_bytes),
-           "roofline": roofline(g_per_kernel, 0.0, pk, src, kv_bytes=g_bytes * share,
+           "roofline": roofline(g_per_kernel, 0.0, pk, src, steps, kv_bytes=g_bytes * share,
                                 workload=f"cfg4_gqa{gq}", scale_units=share),
            "gpu_launches": g_launches,
            "config": f"config 4 geometry with {CFG4['H'] // gq} K/V heads for {CFG4['H']} "
@@ -810,7 +837,7 @@ def bench_decode(dist, args, pk, src):
             "ms_per_step": round(r_ms / steps, 4), "cache_bytes": cache.memory_bytes,
             "full_cache_bytes": full_bytes,
             "memory_ratio": round(full_bytes / cache.memory_bytes, 2),
-            "roofline": roofline(r_per_kernel, 0.0, pk, src, kv_bytes=kv_bytes * share,
+            "roofline": roofline(r_per_kernel, 0.0, pk, src, steps, kv_bytes=kv_bytes * share,
                                  workload="cfg4_ring", scale_units=share),
             "gpu_launches": r_launches}
     del q, k, v, cache
@@ -1013,6 +1040,9 @@ def main():
                            "units_rank0": [start, stop], "units_total": units,
                            "verify_rank0": r["verify"],
                            "per_kernel_ms": {k: round(v[0], 3) for k, v in r["per_kernel"].items()},
+                           "per_kernel_ms_serialised_pass": {
+                               k: round(v[0], 3) for k, v in r["per_kernel_iso"].items()},
+                           "roofline_overlapped_pass": r["roofline_overlapped"],
                            "step_ms_rank0": [round(x, 3) for x in r["step_ms"]],
                            "host_enqueue_ms_rank0": [round(x, 3) for x in r["host_ms"]],
                            "timed_as": r["timing"],
@@ -1021,7 +1051,7 @@ def main():
         ex = executed_mma_flops(mask, CFG2, stop - start,
                                 dq_gemms=1 if "dq_gemm_kernel" in r["per_kernel"] else 3)
         alg = {k: KERNEL_WORK[k] * r["flops_fwd"] * (stop - start) / units for k in ex}
-        extra["fwdbwd"]["mma_flops_per_launch_rank0"] = {
+        extra["fwdbwd"]["mma_flops_per_step_rank0"] = {
             k: {"executed": ex[k], "algorithmic": alg[k], "ratio": round(ex[k] / alg[k], 4)}
             for k in ex}
         if "weak" in r:
