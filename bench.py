@@ -584,6 +584,10 @@ def bench_fwdbwd(dist, args, pk, src):
     if gres is None:
         ms, launches, clk = e_ms, e_launches, eclk
         step_ms, host_ms = list(STEP_MS), list(HOST_MS)
+    else:
+        ms, launches = gres["ms"], gres["launches"]
+        step_ms, host_ms = gres["step_ms"], gres["host_ms"]
+    value = 3.5 * F * args.steps / (ms / 1e3) / 1e12
     # roofline pass: with the dQ GEMM overlapped, dK/dV and dQ share the SMs
     # and each one's CUDA-event duration includes the other's; this eager
     # pass runs one dK/dV pass and then the dQ GEMM, so each duration is the
@@ -597,10 +601,6 @@ def bench_fwdbwd(dist, args, pk, src):
             os.environ.pop("SBFA_BWD_GROUPS", None)
         else:
             os.environ["SBFA_BWD_GROUPS"] = old_groups
-    else:
-        ms, launches = gres["ms"], gres["launches"]
-        step_ms, host_ms = gres["step_ms"], gres["host_ms"]
-    value = 3.5 * F * args.steps / (ms / 1e3) / 1e12
 
     # verification (outside the timed region)
     o = step()
