@@ -1332,8 +1332,10 @@ cudaStream_t dq_side_stream(cudaStream_t s) {
 // and writes only its own rows, so the order between groups does not matter;
 // the caller's stream waits for the side stream before it returns, and a
 // CUDA-graph capture of the caller's stream takes the side stream in and
-// joins it again.  Four groups once the problem has at least 16 items per SM
-// (below that the extra launches cost more than the overlap gains);
+// joins it again.  Four groups once the problem has at least 64 items per SM
+// (at 14-55 per SM the extra launches and group tails cost as much as the
+// overlap gains or more: -0.4 % at 28, -1 % at 55, -24 % at 14 items per SM
+// forced to four groups);
 // SBFA_BWD_GROUPS and SBFA_DQ_GRID override the group count and the dQ
 // GEMM's CTA count (SBFA_BWD_GROUPS=1: one dK/dV pass, then dQ on the
 // caller's stream).
@@ -1346,7 +1348,7 @@ int run_bwd_tc(const void* q, const void* k, const void* v, const void* dout, vo
   const int sms = device_sm_count();
   const int64_t items = (int64_t)ceil_div_i(mp.n_q, kT) * BH;
   int want = env_int("SBFA_BWD_GROUPS", 0);
-  if (want <= 0) want = items >= 16LL * sms ? 4 : 1;
+  if (want <= 0) want = items >= 64LL * sms ? 4 : 1;
   int dq_grid = env_int("SBFA_DQ_GRID", 0);
   if (dq_grid <= 0) dq_grid = std::max(1, sms * 3 / 8);
   const int H = vw.heads, B = BH / H, g = vw.kv_group;

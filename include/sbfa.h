@@ -192,7 +192,7 @@ int sbfa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
  * stores every 16-bit dS tile there and dQ becomes a GEMM over the stored
  * tiles, instead of a third pass that recomputes S, P and dP; NULL keeps that
  * pass.  The two give the same dQ to rounding (the dS values are the dK/dV
- * pass's).  With the stored tiles and a large enough problem (16 or more
+ * pass's).  With the stored tiles and a large enough problem (64 or more
  * 128-row query tiles x B*H per SM) the dQ GEMM of one group of (b, h) units
  * runs on a library-owned high-priority side stream beside the next group's
  * dK/dV pass; the side stream belongs to `stream` (one per device and

@@ -2,7 +2,7 @@
 
 At head_dim 128 the backward cuts the (b, h) units into groups and runs
 group g's dQ GEMM on a high-priority side stream beside group g + 1's dK/dV
-pass (automatic once the problem has 16 query-tile items per SM;
+pass (automatic once the problem has 64 query-tile items per SM;
 ``SBFA_BWD_GROUPS`` forces a group count, 1 switching the overlap off).
 Every group computes exactly what the single pass computes for its units,
 so the results must be bit-identical with and without the overlap, for
