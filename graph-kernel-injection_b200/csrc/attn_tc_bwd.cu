@@ -1256,6 +1256,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
     // persistent: one CTA per SM (or dq_grid CTAs) over the (query tile,
     // query (b, h)) items
     const int64_t items = (int64_t)ceil_div_i(mp.n_q, kT) * BH;
+    if (items >= (1LL << 31))  // the kernel counts items in 32-bit integers
+      return fail(SBFA_ERR_UNSUPPORTED, "dQ GEMM: B * H * ceil(n_q / 128) must be < 2^31");
     const int cap = dq_grid > 0 ? std::min(dq_grid, device_sm_count()) : device_sm_count();
     const int grid = (int)std::min<int64_t>(items, cap);
     LaunchScope ls("dq_gemm_kernel", sq);
