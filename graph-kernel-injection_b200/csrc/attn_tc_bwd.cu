@@ -1365,7 +1365,8 @@ int run_bwd_tc(const void* q, const void* k, const void* v, const void* dout, vo
   Views vg = vw;
   vg.heads = Hg;
   const int64_t es = (int64_t)sizeof(T);
-  for (int bi = 0; bi < B; ++bi) {
+  int rc_groups = SBFA_OK;
+  for (int bi = 0; bi < B && rc_groups == SBFA_OK; ++bi) {
     for (int hs = 0; hs < hsplit; ++hs) {
       const int h0 = hs * Hg;
       const int64_t u = (int64_t)bi * H + h0;  // the group's first query (b, h)
@@ -1381,17 +1382,24 @@ int run_bwd_tc(const void* q, const void* k, const void* v, const void* dout, vo
               part_ws != nullptr ? part_ws + (u / g) * sink_parts * 2 * kT * D : nullptr,
               sink_parts, csc_pos, nnz,
               static_cast<char*>(ds_ws) + u * nnz * (int64_t)(kT * kT * 2), status, s, side,
-              last ? 0 : dq_grid))
-        return rc;
+              last ? 0 : dq_grid)) {
+        rc_groups = rc;
+        break;
+      }
     }
   }
+  // join even after a failed launch, so that nothing queued on the side
+  // stream outlives the call unordered with the caller's stream
   cudaEvent_t ev = nullptr;
-  if (int rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming),
-                          "cudaEventCreateWithFlags"))
-    return rc;
-  cudaError_t e = cudaEventRecord(ev, side);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev, 0);
-  cudaEventDestroy(ev);
+  cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) {
+    e = cudaEventRecord(ev, side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev, 0);
+    cudaEventDestroy(ev);
+  } else {
+    e = cudaStreamSynchronize(side);  // no event to order with: wait for it here
+  }
+  if (rc_groups != SBFA_OK) return rc_groups;
   return check_cuda(e, "dQ side stream: join");
 }
 
